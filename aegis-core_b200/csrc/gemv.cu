@@ -1,0 +1,396 @@
+// Decode GEMV family (gemv_*): C[M,N] = alpha * A[M,K] * B[K,N] + beta * C for
+// small M, memory-bound on the weights B.
+//
+// Replaces the reference's decode kernels (src/gemm/gemv.cu:105-236 and the
+// mma.sync gemv_tc.cu:152-197) with a B200 streaming design on CUDA cores:
+//   - CTA = 256 threads over a BN-column x MT-row output tile and one K slice
+//     (split-K). LPR = BN/8 lanes cover one B row with 16-byte loads (8
+//     elements each), so a warp reads 32/LPR rows x BN*2 contiguous bytes per
+//     load instruction; the RG = 256/LPR row groups stride down the slice.
+//     U independent 16-byte loads per thread are in flight before any math.
+//   - A's slice rows are staged in shared memory as FP32 [k][MT] (chunks of
+//     KCH rows), read as broadcasts.
+//   - FP32 FMA into MT x 8 accumulators per thread, k ascending.
+//   - Reduction: row groups inside a warp by a fixed shuffle-xor tree, then
+//     the 8 warps through shared memory in warp order 0..7.
+//   - Split-K, deterministic (reference src/gemm/splitk.cuh:155-222): every
+//     CTA of a tile writes its FP32 partial slot, fences, takes a ticket on
+//     the tile's counter; the CTA that draws the last ticket sums slots
+//     0..S-1 in order, applies alpha/beta, and resets the counter to 0.
+//     Nothing waits on another CTA.
+// No tensor cores: the shape is memory-bound.
+#include <algorithm>
+
+#include "common.cuh"
+#include "device.h"
+#include "kernels.h"
+#include "workspace.h"
+
+namespace aegis {
+
+using gemm::DType;
+using gemm::GemmParams;
+using gemm::Layout;
+
+namespace {
+
+constexpr int GThreads = 256;
+constexpr int kSmemFloats = 8192;  // 32 KiB: A chunk, then the cross-warp reduction (aliased)
+constexpr int kMinSplitRows = 128;
+
+struct GemvArgs {
+  const void* A;
+  const void* B;
+  void* C;
+  int M, N, K;
+  int ra;                    // A row-major
+  long long lda, ldb, ldc, sa, sb, sc;
+  float alpha, beta;
+  int tiles_n, tiles_m;
+  int S, kc;                 // splits, rows per split
+  unsigned* counters;        // per tile (S > 1)
+  float* partials;           // tiles x S x MT x BN (S > 1)
+  int batch0;
+};
+
+template <int MT>
+__device__ __forceinline__ void fma8(float (&acc)[MT][8], const float (&b)[8], const float* arow) {
+#pragma unroll
+  for (int m = 0; m < MT; ++m) {
+    const float av = arow[m];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[m][j] = fmaf(av, b[j], acc[m][j]);
+  }
+}
+
+template <class T>
+__device__ __forceinline__ void unpack8(const uint4& v, float (&b)[8]) {
+  using E = Elem<T>;
+  const float2 p0 = E::pair_to_f32(v.x), p1 = E::pair_to_f32(v.y), p2 = E::pair_to_f32(v.z),
+               p3 = E::pair_to_f32(v.w);
+  b[0] = p0.x; b[1] = p0.y; b[2] = p1.x; b[3] = p1.y;
+  b[4] = p2.x; b[5] = p2.y; b[6] = p3.x; b[7] = p3.y;
+}
+
+// VECB: B row-major with 16-byte-aligned rows (base, ldb); otherwise element loads.
+template <class T, int LPR, int MT, bool VECB>
+__global__ void __launch_bounds__(GThreads) gemv_kernel(GemvArgs a) {
+  using E = Elem<T>;
+  constexpr int BN = 8 * LPR;
+  constexpr int RG = GThreads / LPR;
+  constexpr int KCH = kSmemFloats / MT;                  // A rows staged per chunk
+  constexpr int U = MT >= 8 ? 2 : (MT >= 4 ? 4 : 8);     // loads in flight per thread
+  static_assert(8 * MT * BN <= kSmemFloats, "cross-warp reduction must fit the shared buffer");
+  __shared__ __align__(16) float sm[kSmemFloats];
+  __shared__ int s_last;
+
+  const int tid = int(threadIdx.x);
+  const int l = tid % LPR, g = tid / LPR;
+  const int split = int(blockIdx.x % a.S);
+  const int nt = int(blockIdx.x / a.S);
+  const int mt = int(blockIdx.y);
+  const long long b = a.batch0 + blockIdx.z;
+  const int n0 = nt * BN, m0 = mt * MT;
+  const int k_begin = split * a.kc;
+  const int k_end = min(a.K, k_begin + a.kc);
+  const T* A = static_cast<const T*>(a.A) + b * a.sa;
+  const T* B = static_cast<const T*>(a.B) + b * a.sb;
+  const int n = n0 + l * 8;  // first of this thread's 8 columns
+  const int ncols = max(0, min(8, a.N - n));
+
+  float acc[MT][8];
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[m][j] = 0.f;
+
+  for (int c0 = k_begin; c0 < k_end; c0 += KCH) {
+    const int clen = min(KCH, k_end - c0);
+    __syncthreads();  // previous chunk fully consumed
+    for (int i = tid; i < clen * MT; i += GThreads) {
+      const int kk = i / MT, m = i % MT;
+      const int gm = m0 + m, gk = c0 + kk;
+      float v = 0.f;
+      if (gm < a.M) v = E::to_f32(a.ra ? A[(long long)gm * a.lda + gk] : A[gm + (long long)gk * a.lda]);
+      sm[kk * MT + m] = v;
+    }
+    __syncthreads();
+    for (int kk = g; kk < clen; kk += RG * U) {
+      uint4 bv[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int k = kk + u * RG;
+        bv[u] = make_uint4(0u, 0u, 0u, 0u);
+        if (k < clen && ncols > 0) {
+          const long long gk = c0 + k;
+          if constexpr (VECB) {
+            const T* src = B + gk * a.ldb + n;
+            if (ncols == 8) {
+              bv[u] = __ldg(reinterpret_cast<const uint4*>(src));
+            } else {
+              uint16_t h[8] = {};
+              for (int j = 0; j < ncols; ++j) h[j] = reinterpret_cast<const uint16_t*>(src)[j];
+              bv[u] = make_uint4(h[0] | (uint32_t(h[1]) << 16), h[2] | (uint32_t(h[3]) << 16),
+                                 h[4] | (uint32_t(h[5]) << 16), h[6] | (uint32_t(h[7]) << 16));
+            }
+          } else {
+            uint16_t h[8] = {};
+            for (int j = 0; j < ncols; ++j) {
+              const T* src = B + gk + (long long)(n + j) * a.ldb;  // column-major (or misaligned) B
+              h[j] = *reinterpret_cast<const uint16_t*>(src);
+            }
+            bv[u] = make_uint4(h[0] | (uint32_t(h[1]) << 16), h[2] | (uint32_t(h[3]) << 16),
+                               h[4] | (uint32_t(h[5]) << 16), h[6] | (uint32_t(h[7]) << 16));
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int k = kk + u * RG;
+        if (k < clen) {
+          float bf[8];
+          unpack8<T>(bv[u], bf);
+          fma8<MT>(acc, bf, &sm[k * MT]);
+        }
+      }
+    }
+  }
+
+  // Row groups inside the warp: fixed shuffle-xor tree over the lane bits above LPR.
+#pragma unroll
+  for (int off = LPR; off < 32; off <<= 1)
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[m][j] += __shfl_xor_sync(0xffffffffu, acc[m][j], off);
+
+  // The 8 warps through shared memory, summed in warp order.
+  __syncthreads();  // A chunk no longer needed: reuse the buffer
+  const int warp = tid / 32, wl = tid % 32;
+  if (wl < LPR) {
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) sm[(warp * MT + m) * BN + wl * 8 + j] = acc[m][j];
+  }
+  __syncthreads();
+  constexpr int ELEMS = MT * BN;
+  float tilev[ceil_div(ELEMS, GThreads)];
+#pragma unroll
+  for (int r = 0; r < ceil_div(ELEMS, GThreads); ++r) {
+    const int e = tid + r * GThreads;
+    float s = 0.f;
+    if (e < ELEMS) {
+      s = sm[e];
+#pragma unroll
+      for (int w = 1; w < 8; ++w) s += sm[w * ELEMS + e];
+    }
+    tilev[r] = s;
+  }
+
+  T* C = static_cast<T*>(a.C) + b * a.sc;
+  auto store = [&](int e, float v) {
+    const int m = e / BN, c = e % BN;
+    const int gm = m0 + m, gn = n0 + c;
+    if (gm >= a.M || gn >= a.N) return;
+    T* q = C + (long long)gm * a.ldc + gn;
+    float x = a.alpha * v;
+    if (a.beta != 0.f) x += a.beta * E::to_f32(*q);
+    *q = E::from_f32(x);
+  };
+
+  if (a.S == 1) {
+#pragma unroll
+    for (int r = 0; r < ceil_div(ELEMS, GThreads); ++r) {
+      const int e = tid + r * GThreads;
+      if (e < ELEMS) store(e, tilev[r]);
+    }
+    return;
+  }
+  const long long tile = ((long long)blockIdx.z * a.tiles_m + mt) * a.tiles_n + nt;
+  float* slot0 = a.partials + tile * a.S * ELEMS;
+#pragma unroll
+  for (int r = 0; r < ceil_div(ELEMS, GThreads); ++r) {
+    const int e = tid + r * GThreads;
+    if (e < ELEMS) __stcg(slot0 + (long long)split * ELEMS + e, tilev[r]);
+  }
+  __threadfence();  // the partial is visible device-wide before the ticket
+  __syncthreads();
+  if (tid == 0) s_last = atomicAdd(a.counters + tile, 1u) == unsigned(a.S - 1);
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();  // acquire the other CTAs' partials
+#pragma unroll
+  for (int r = 0; r < ceil_div(ELEMS, GThreads); ++r) {
+    const int e = tid + r * GThreads;
+    if (e >= ELEMS) continue;
+    float s = __ldcg(slot0 + e);
+    for (int q = 1; q < a.S; ++q) s += __ldcg(slot0 + (long long)q * ELEMS + e);
+    store(e, s);
+  }
+  if (tid == 0) a.counters[tile] = 0;  // ready for the next launch (graph replays need no reset)
+}
+
+// --------------------------------------------------------------- host side
+int mt_for(int M, int BN) {
+  const int cap = 1024 / BN;  // MT * BN <= 1024 (reduction buffer)
+  int mt = 1;
+  while (mt < M && mt < 16 && mt < cap) mt <<= 1;
+  return mt;
+}
+
+struct GPlan {
+  int LPR, MT, S, kc, tiles_n, tiles_m;
+  long long tiles;
+};
+
+GPlan plan_for(int cfg, const GemmParams& p) {
+  const gemm::GemvConfig& c = gemm::GEMV_CONFIGS[cfg];
+  GPlan pl{};
+  pl.LPR = c.BN / 8;
+  pl.MT = mt_for(p.M, c.BN);
+  pl.tiles_n = ceil_div(p.N, c.BN);
+  pl.tiles_m = ceil_div(p.M, pl.MT);
+  pl.tiles = (long long)pl.tiles_n * pl.tiles_m * p.batch;
+  const hw::DeviceLimits* d = hw::current();
+  const int sms = d ? d->sm_count : 0;
+  // Enough CTAs for ~4 resident per SM (bytes in flight), splits at least
+  // kMinSplitRows long, partials bounded by the workspace cap.
+  int S = 1;
+  if (sms > 0) {
+    const long long target = (long long)sms * 4;
+    const long long want = (target + pl.tiles - 1) / pl.tiles;
+    const long long smax = std::max(1, p.K / kMinSplitRows);
+    const long long cap = std::max<long long>(
+        1, gemm::kSplitKMaxWorkspace / std::max<long long>(1, pl.tiles * pl.MT * c.BN * (long long)sizeof(float)));
+    S = int(std::max<long long>(1, std::min({want, smax, cap})));
+  }
+  int kc = ceil_div(ceil_div(p.K, S), 16) * 16;
+  S = ceil_div(p.K, kc);
+  if (S == 1) kc = p.K;
+  pl.S = S;
+  pl.kc = kc;
+  return pl;
+}
+
+bool vec_b_ok(const GemmParams& p) {
+  return p.layout_b == Layout::RowMajor && (reinterpret_cast<uintptr_t>(p.B) & 15u) == 0 && p.ldb % 8 == 0 &&
+         (p.batch <= 1 || p.stride_b % 8 == 0);
+}
+
+template <class T, int LPR, int MT, bool VECB>
+cudaError_t launch_t(const GemvArgs& a, dim3 grid, cudaStream_t s) {
+  gemv_kernel<T, LPR, MT, VECB><<<grid, GThreads, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+template <class T, int LPR, bool VECB>
+cudaError_t launch_mt(int MT, const GemvArgs& a, dim3 grid, cudaStream_t s) {
+  switch (MT) {
+    case 1: return launch_t<T, LPR, 1, VECB>(a, grid, s);
+    case 2: return launch_t<T, LPR, 2, VECB>(a, grid, s);
+    case 4: return launch_t<T, LPR, 4, VECB>(a, grid, s);
+    case 8:
+      if constexpr (LPR <= 16) return launch_t<T, LPR, 8, VECB>(a, grid, s);
+      break;
+    case 16:
+      if constexpr (LPR <= 8) return launch_t<T, LPR, 16, VECB>(a, grid, s);
+      break;
+  }
+  return cudaErrorInvalidValue;
+}
+
+template <class T, bool VECB>
+cudaError_t launch_lpr(int LPR, int MT, const GemvArgs& a, dim3 grid, cudaStream_t s) {
+  switch (LPR) {
+    case 32: return launch_mt<T, 32, VECB>(MT, a, grid, s);
+    case 16: return launch_mt<T, 16, VECB>(MT, a, grid, s);
+    case 8: return launch_mt<T, 8, VECB>(MT, a, grid, s);
+    case 4: return launch_mt<T, 4, VECB>(MT, a, grid, s);
+  }
+  return cudaErrorInvalidValue;
+}
+
+template <class T>
+cudaError_t launch_all(bool vec, int LPR, int MT, const GemvArgs& a, dim3 grid, cudaStream_t s) {
+  return vec ? launch_lpr<T, true>(LPR, MT, a, grid, s) : launch_lpr<T, false>(LPR, MT, a, grid, s);
+}
+
+constexpr int kMaxGridZ = 65535;
+
+}  // namespace
+
+cudaError_t gemv_run(int cfg, const GemmParams& p, cudaStream_t stream) {
+  if (const cudaError_t e = gemm::validate(p); e != cudaSuccess) return e;
+  if (gemm::is_empty(p)) return cudaSuccess;
+  if (p.alpha == 0.f) return scale_c(p, stream);
+  const GPlan pl = plan_for(cfg, p);
+  if (pl.tiles_m > 65535) return cudaErrorInvalidConfiguration;
+  GemvArgs a{};
+  a.A = p.A;
+  a.B = p.B;
+  a.C = p.C;
+  a.M = p.M;
+  a.N = p.N;
+  a.K = p.K;
+  a.ra = p.layout_a == Layout::RowMajor;
+  a.lda = p.lda;
+  a.ldb = p.ldb;
+  a.ldc = p.ldc;
+  a.sa = p.stride_a;
+  a.sb = p.stride_b;
+  a.sc = p.stride_c;
+  a.alpha = p.alpha;
+  a.beta = p.beta;
+  a.tiles_n = pl.tiles_n;
+  a.tiles_m = pl.tiles_m;
+  a.S = pl.S;
+  a.kc = pl.kc;
+  const long long grid_x = (long long)pl.tiles_n * pl.S;
+  if (grid_x > 0x7fffffffll) return cudaErrorInvalidConfiguration;
+  const bool vec = vec_b_ok(p);
+  for (int b0 = 0; b0 < p.batch; b0 += kMaxGridZ) {
+    const int nb = std::min(kMaxGridZ, p.batch - b0);
+    a.batch0 = b0;
+    if (pl.S > 1) {
+      // Tile indices restart per launch (blockIdx.z), so each launch of a
+      // batch chunk reuses the same counter/partial slots, in stream order.
+      const long long tiles = (long long)pl.tiles_n * pl.tiles_m * nb;
+      void* cnt = nullptr;
+      void* part = nullptr;
+      if (const cudaError_t e = ws::get(stream, size_t(tiles) * sizeof(unsigned), &cnt, ws::Use::SplitKCounters);
+          e != cudaSuccess)
+        return e;
+      const size_t pbytes = size_t(tiles) * pl.S * pl.MT * (8 * pl.LPR) * sizeof(float);
+      if (const cudaError_t e = ws::get(stream, pbytes, &part, ws::Use::SplitKPartials); e != cudaSuccess) return e;
+      a.counters = static_cast<unsigned*>(cnt);
+      a.partials = static_cast<float*>(part);
+    }
+    const dim3 grid(unsigned(grid_x), unsigned(pl.tiles_m), unsigned(nb));
+    const cudaError_t e = p.dtype == DType::BF16 ? launch_all<__nv_bfloat16>(vec, pl.LPR, pl.MT, a, grid, stream)
+                                                 : launch_all<__half>(vec, pl.LPR, pl.MT, a, grid, stream);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+gemm::LaunchPlan gemv_plan(int cfg, const GemmParams& p) {
+  const GPlan pl = plan_for(cfg, p);
+  gemm::LaunchPlan r;
+  r.splits = pl.S;
+  r.k_chunk = pl.kc;
+  r.tiles = pl.tiles;
+  r.grid = unsigned((long long)pl.tiles_n * pl.S * pl.tiles_m * p.batch);
+  return r;
+}
+
+cudaError_t gemv_attrs(int cfg, cudaFuncAttributes* attrs) {
+  switch (gemm::GEMV_CONFIGS[cfg].BN / 8) {
+    case 32: return cudaFuncGetAttributes(attrs, &gemv_kernel<__half, 32, 1, true>);
+    case 16: return cudaFuncGetAttributes(attrs, &gemv_kernel<__half, 16, 1, true>);
+    case 8: return cudaFuncGetAttributes(attrs, &gemv_kernel<__half, 8, 1, true>);
+    default: return cudaFuncGetAttributes(attrs, &gemv_kernel<__half, 4, 1, true>);
+  }
+}
+
+}  // namespace aegis

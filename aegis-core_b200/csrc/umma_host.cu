@@ -1,0 +1,314 @@
+// Host side of the umma family: TMA tensor maps, the split-K plan, the
+// deterministic split-K reduction kernel, and the run() entry points.
+//
+// Split-K (tall-K shapes whose tiles cannot fill the SMs): S CTAs per output
+// tile each run the same main loop over a K slice and write FP32 partials to
+// workspace slot s ([s][batch][M][N]); a second kernel sums slots 0..S-1 in
+// that fixed order per element and applies alpha/beta. Results are bitwise
+// identical run to run. The reference gets the same guarantee with an
+// ordered ticket in the last CTA of each tile (src/gemm/splitk.cuh:155-222);
+// with 128x256 tiles and up to ~74 splits the last CTA would read megabytes
+// alone, so here every SM shares the (L2-resident) reduction.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+#include "device.h"
+#include "kernels.h"
+#include "status.h"
+#include "umma_launch.cuh"
+#include "workspace.h"
+
+namespace aegis {
+
+using gemm::DType;
+using gemm::GemmParams;
+using gemm::Layout;
+
+int splitk_choose(long long tiles, int k_blocks, int sms, int min_blocks_per_split, double t_block_ns,
+                  double reduce_ns_per_split, long long max_splits) {
+  if (sms < 1 || tiles < 1 || k_blocks < 1) return 1;
+  long long s_max = k_blocks / std::max(1, min_blocks_per_split);
+  s_max = std::min<long long>(s_max, max_splits);
+  s_max = std::min<long long>(s_max, 1024);
+  if (s_max < 1) s_max = 1;
+  int best = 1;
+  double best_cost = 0;
+  for (long long S = 1; S <= s_max; ++S) {
+    const long long kc = (k_blocks + S - 1) / S;
+    const long long s_eff = (k_blocks + kc - 1) / kc;  // splits actually launched
+    if (s_eff != S) continue;
+    const long long waves = (tiles * S + sms - 1) / sms;
+    const double cost = double(waves) * double(kc) * t_block_ns + (S > 1 ? double(S) * reduce_ns_per_split : 0.0);
+    if (S == 1 || cost < best_cost) {
+      best = int(S);
+      best_cost = cost;
+    }
+  }
+  return best;
+}
+
+namespace {
+
+// ---------------------------------------------------------------- tensor maps
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      cudaGetLastError();
+      p = nullptr;
+    }
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+
+// A 3-D (inner, outer, batch) 16-bit tensor, 128-byte swizzled boxes of
+// {64, box_outer, 1}. ld and batch stride in elements.
+bool encode_map(CUtensorMap* map, DType dt, const void* base, long long inner, long long outer, long long ld,
+                long long batch, long long bstride, int box_outer) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  if (batch <= 1) {
+    batch = 1;
+    bstride = ((outer * ld + 7) / 8) * 8;  // unused coordinate; any legal stride
+  }
+  cuuint64_t dims[3] = {cuuint64_t(inner), cuuint64_t(outer), cuuint64_t(batch)};
+  cuuint64_t strides[2] = {cuuint64_t(ld) * 2, cuuint64_t(bstride) * 2};
+  cuuint32_t box[3] = {64, cuuint32_t(box_outer), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  const CUtensorMapDataType t =
+      dt == DType::BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUresult r = fn(map, t, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+struct Maps {
+  CUtensorMap a, b;
+};
+
+// A: row-major -> K-major box {64 k, 128 m}; col-major -> M-major boxes {64 m, 64 k}.
+// B: row-major -> N-major boxes {64 n, 64 k}; col-major -> K-major box {64 k, BN n}.
+bool make_maps(const GemmParams& p, int BN, Maps* m) {
+  const bool ar = p.layout_a == Layout::RowMajor, br = p.layout_b == Layout::RowMajor;
+  const long long ba = p.batch > 1 && p.stride_a != 0 ? p.batch : 1;
+  const long long bb = p.batch > 1 && p.stride_b != 0 ? p.batch : 1;
+  const bool okA = ar ? encode_map(&m->a, p.dtype, p.A, p.K, p.M, p.lda, ba, p.stride_a, umma::BM)
+                      : encode_map(&m->a, p.dtype, p.A, p.M, p.K, p.lda, ba, p.stride_a, umma::BK);
+  const bool okB = br ? encode_map(&m->b, p.dtype, p.B, p.N, p.K, p.ldb, bb, p.stride_b, umma::BK)
+                      : encode_map(&m->b, p.dtype, p.B, p.K, p.N, p.ldb, bb, p.stride_b, BN);
+  return okA && okB;
+}
+
+// ---------------------------------------------------------------- split-K reduce
+// out[b][m][n] = alpha * (P[0] + P[1] + ... + P[S-1]) (+ beta * C), summed in
+// split order. Four columns per thread when N % 4 == 0.
+template <class T, bool VEC4>
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ part, int S, int batch, int M,
+                                                            int N, T* __restrict__ C, long long ldc,
+                                                            long long stride_c, float alpha, float beta) {
+  using E = Elem<T>;
+  const long long plane = (long long)batch * M * N;
+  constexpr int W = VEC4 ? 4 : 1;
+  const int nw = N / W;
+  const long long total = (long long)batch * M * nw;
+  for (long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x; t < total;
+       t += (long long)gridDim.x * blockDim.x) {
+    const int n = int(t % nw) * W;
+    const long long bm = t / nw;
+    const int m = int(bm % M), b = int(bm / M);
+    const long long off = bm * N + n;
+    T* c = C + b * stride_c + (long long)m * ldc + n;
+    if constexpr (VEC4) {
+      float4 acc = __ldcg(reinterpret_cast<const float4*>(part + off));
+      for (int s = 1; s < S; ++s) {
+        const float4 q = __ldcg(reinterpret_cast<const float4*>(part + s * plane + off));
+        acc.x += q.x; acc.y += q.y; acc.z += q.z; acc.w += q.w;
+      }
+      float v[4] = {alpha * acc.x, alpha * acc.y, alpha * acc.z, alpha * acc.w};
+      if (beta != 0.f)
+        for (int j = 0; j < 4; ++j) v[j] += beta * E::to_f32(c[j]);
+      if ((reinterpret_cast<uintptr_t>(c) & 7u) == 0) {
+        uint2 w;
+        w.x = E::pack(v[0], v[1]);
+        w.y = E::pack(v[2], v[3]);
+        *reinterpret_cast<uint2*>(c) = w;
+      } else {
+        for (int j = 0; j < 4; ++j) c[j] = E::from_f32(v[j]);
+      }
+    } else {
+      float acc = __ldcg(part + off);
+      for (int s = 1; s < S; ++s) acc += __ldcg(part + s * plane + off);
+      float v = alpha * acc;
+      if (beta != 0.f) v += beta * E::to_f32(*c);
+      *c = E::from_f32(v);
+    }
+  }
+}
+
+template <class T>
+cudaError_t launch_reduce(const float* part, int S, const GemmParams& p, cudaStream_t s) {
+  const hw::DeviceLimits* d = hw::physical();
+  const int sms = d ? d->sm_count : 148;
+  const bool vec = p.N % 4 == 0;
+  const long long total = (long long)p.batch * p.M * (vec ? p.N / 4 : p.N);
+  const int blocks = int(std::max<long long>(1, std::min<long long>((total + 255) / 256, (long long)sms * 8)));
+  T* C = static_cast<T*>(p.C);
+  if (vec)
+    splitk_reduce_kernel<T, true><<<blocks, 256, 0, s>>>(part, S, p.batch, p.M, p.N, C, p.ldc, p.stride_c, p.alpha,
+                                                          p.beta);
+  else
+    splitk_reduce_kernel<T, false><<<blocks, 256, 0, s>>>(part, S, p.batch, p.M, p.N, C, p.ldc, p.stride_c, p.alpha,
+                                                           p.beta);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------- planning
+struct Plan {
+  int BN = 256, STAGES = 4;
+  int splits = 1, kb_per_split = 0, kb_total = 0;
+  int tiles_m = 0, tiles_n = 0;
+  long long tiles = 0, units = 0;
+  int grid = 0;
+};
+
+Plan make_plan(int cfg, const GemmParams& p) {
+  const gemm::UmmaConfig& c = gemm::UMMA_CONFIGS[cfg];
+  Plan pl;
+  pl.BN = c.BN;
+  pl.STAGES = c.STAGES;
+  pl.tiles_m = ceil_div(p.M, umma::BM);
+  pl.tiles_n = ceil_div(p.N, c.BN);
+  pl.kb_total = ceil_div(p.K, umma::BK);
+  pl.tiles = (long long)p.batch * pl.tiles_m * pl.tiles_n;
+  const hw::DeviceLimits* d = hw::current();
+  const int sms = d ? d->sm_count : 0;
+  int S = 1;
+  if (c.SPLITK && sms > 0 && pl.tiles < sms) {
+    // One k-block is BK/16 = 4 MMAs of 128 x BN x 16 (about 128 cycles each at
+    // BN = 256 on one SM, ~1.85 GHz). The reduction moves 8 bytes per output
+    // element per split (write + read FP32) at ~5 TB/s.
+    const double t_block_ns = 4.0 * 128.0 * (double(c.BN) / 256.0) / 1.85;
+    const double out_elems = double(p.batch) * p.M * p.N;
+    const double reduce_ns = out_elems * 8.0 / 5.0e3;
+    const long long cap = std::max<long long>(1, gemm::kSplitKMaxWorkspace / (long long)std::max(1.0, out_elems * 4));
+    S = splitk_choose(pl.tiles, pl.kb_total, sms, 4, t_block_ns, reduce_ns, cap);
+  }
+  pl.kb_per_split = ceil_div(pl.kb_total, S);
+  pl.splits = ceil_div(pl.kb_total, pl.kb_per_split);
+  pl.units = pl.tiles * pl.splits;
+  const long long g = sms > 0 ? std::min<long long>(pl.units, sms) : pl.units;
+  pl.grid = int(std::max<long long>(1, g));
+  return pl;
+}
+
+umma::Args make_args(const GemmParams& p, const Plan& pl) {
+  umma::Args a{};
+  a.M = p.M;
+  a.N = p.N;
+  a.K = p.K;
+  a.batch = p.batch;
+  a.a_batched = p.batch > 1 && p.stride_a != 0;
+  a.b_batched = p.batch > 1 && p.stride_b != 0;
+  a.tiles_m = pl.tiles_m;
+  a.tiles_n = pl.tiles_n;
+  a.splits = pl.splits;
+  a.kb_per_split = pl.kb_per_split;
+  a.kb_total = pl.kb_total;
+  a.units = pl.units;
+  a.C = p.C;
+  a.ldc = p.ldc;
+  a.stride_c = p.stride_c;
+  a.alpha = p.alpha;
+  a.beta = p.beta;
+  a.wait_limit_ns = kDefaultWaitLimitNs;
+  return a;
+}
+
+cudaError_t launch(const GemmParams& p, const umma::LaunchKey& k, const Maps& m, const umma::Args& a, int grid,
+                   cudaStream_t s) {
+  return p.dtype == DType::BF16 ? umma::launch_family<__nv_bfloat16>(k, m.a, m.b, a, grid, s)
+                                : umma::launch_family<__half>(k, m.a, m.b, a, grid, s);
+}
+
+bool device_is_sm100() {
+  const hw::DeviceLimits* d = hw::physical();
+  return d && d->arch == 100;
+}
+
+}  // namespace
+
+cudaError_t umma_run(int cfg, const GemmParams& p, cudaStream_t stream) {
+  if (const cudaError_t e = gemm::validate(p); e != cudaSuccess) return e;
+  if (gemm::is_empty(p)) return cudaSuccess;
+  if (p.alpha == 0.f) return scale_c(p, stream);
+  if (!gemm::tma_compatible(p) || !device_is_sm100()) return simt_run(p, stream);
+  const Plan pl = make_plan(cfg, p);
+  Maps maps;
+  if (!make_maps(p, pl.BN, &maps)) return simt_run(p, stream);  // TMA refused the operand geometry
+  umma::Args a = make_args(p, pl);
+  if (const cudaError_t e = status::word(&a.status); e != cudaSuccess) return e;
+  umma::LaunchKey k{pl.BN, pl.STAGES, p.layout_a == Layout::ColMajor, p.layout_b == Layout::RowMajor,
+                    umma::kEpiStore};
+  if (pl.splits == 1) return launch(p, k, maps, a, pl.grid, stream);
+  // Split-K: partials, then the ordered reduction.
+  void* part = nullptr;
+  const size_t bytes = size_t(pl.splits) * p.batch * size_t(p.M) * p.N * sizeof(float);
+  if (const cudaError_t e = ws::get(stream, bytes, &part, ws::Use::SplitKPartials); e != cudaSuccess) return e;
+  a.partials = static_cast<float*>(part);
+  k.epi = umma::kEpiPartial;
+  if (const cudaError_t e = launch(p, k, maps, a, pl.grid, stream); e != cudaSuccess) return e;
+  return p.dtype == DType::BF16 ? launch_reduce<__nv_bfloat16>(a.partials, pl.splits, p, stream)
+                                : launch_reduce<__half>(a.partials, pl.splits, p, stream);
+}
+
+gemm::LaunchPlan umma_plan(int cfg, const GemmParams& p) {
+  const Plan pl = make_plan(cfg, p);
+  gemm::LaunchPlan r;
+  r.splits = pl.splits;
+  r.k_chunk = pl.kb_per_split * umma::BK;
+  r.tiles = pl.tiles;
+  r.grid = unsigned(pl.grid);
+  return r;
+}
+
+cudaError_t umma_attrs(int cfg, cudaFuncAttributes* attrs) {
+  const gemm::UmmaConfig& c = gemm::UMMA_CONFIGS[cfg];
+  return umma::attrs_family<__half>(c.BN, c.STAGES, attrs);
+}
+
+size_t umma_smem_bytes(int cfg) {
+  const gemm::UmmaConfig& c = gemm::UMMA_CONFIGS[cfg];
+  return c.BN == 256 ? size_t(umma::Layout<256, 4>::ALLOC) : size_t(umma::Layout<128, 6>::ALLOC);
+}
+
+cudaError_t umma_nsharded(const GemmParams& local, void* const* c_ranks, int nranks, int col_offset,
+                          cudaStream_t stream) {
+  if (nranks < 1 || nranks > umma::kMaxPeers || !c_ranks) return cudaErrorInvalidValue;
+  if (!gemm::tma_compatible(local) || !device_is_sm100()) return cudaErrorNotSupported;
+  if (local.layout_a != Layout::RowMajor || local.layout_b != Layout::RowMajor || local.batch != 1)
+    return cudaErrorInvalidValue;
+  const Plan pl = make_plan(0, local);  // 128 x 256 tiles, no split
+  Maps maps;
+  if (!make_maps(local, pl.BN, &maps)) return cudaErrorNotSupported;
+  umma::Args a = make_args(local, pl);
+  if (const cudaError_t e = status::word(&a.status); e != cudaSuccess) return e;
+  a.npeers = nranks;
+  a.col_offset = col_offset;
+  for (int i = 0; i < nranks; ++i) {
+    if (!c_ranks[i]) return cudaErrorInvalidValue;
+    a.peers[i] = c_ranks[i];
+  }
+  const umma::LaunchKey k{pl.BN, pl.STAGES, false, true, umma::kEpiPeers};
+  return launch(local, k, maps, a, pl.grid, stream);
+}
+
+}  // namespace aegis

@@ -1,0 +1,372 @@
+#pragma once
+// The tcgen05 GEMM kernel (umma family).
+//
+// C[M,N] (+)= A[M,K] * B[K,N] for one batch entry per tile, f16 or bf16
+// operands, FP32 accumulation in tensor memory (TMEM).
+//
+// Replaces the reference's best large-GEMM kernel, gemm_mma_tma_kernel
+// (src/gemm/mma_tma.cu:171-228: TMA box loads into an mbarrier ring feeding
+// mma.sync from every warp), with the Blackwell structure:
+//   warp 0      TMA producer: one elected lane fills a STAGES-deep ring of
+//               (A tile, B tile) k-blocks, mbarrier complete_tx;
+//   warp 1      allocates 2*BN TMEM columns; one lane issues tcgen05.mma
+//               (M=128, N=BN, K=16) for every k-block and commits each stage
+//               back to the producer and each finished accumulator to the
+//               epilogue;
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator (warp w reads TMEM
+//               lanes 32*(w%4)..+31, i.e. tile rows), FP32 -> alpha/beta ->
+//               16-bit, stores to C; or FP32 partials (split-K); or the same
+//               16-bit tile stored to every rank's C (N-sharded all-gather).
+// Persistent: gridDim.x <= #SMs CTAs, each walks units blockIdx.x,
+// +gridDim.x, ... in a grouped raster (8 M-tiles per group) so concurrently
+// running tiles share A and B in L2. Two TMEM accumulators let the epilogue
+// of one tile overlap the main loop of the next.
+//
+// Operand layouts in shared memory (128-byte swizzle, TMA writes them):
+//   A row-major  (K-major): one box [128 rows][64 k]          16 KB
+//   A col-major  (M-major): two boxes [64 k][64 m]             2 x 8 KB
+//   B row-major  (N-major): BN/64 boxes [64 k][64 n]           BN/64 x 8 KB
+//   B col-major  (K-major): one box [BN rows n][64 k]          BN*128 B
+// Edges: TMA zero-fills out-of-range rows/columns/k (so K tails add zeros);
+// the epilogue masks rows >= M and columns >= N.
+//
+// Every wait is bounded (ptx::mbar_wait_bounded): on expiry the CTA records
+// a status bit, every role stops waiting, in-flight TMA copies and MMAs are
+// drained (bounded), TMEM is freed, and the kernel returns.
+#include <cuda.h>
+
+#include <cstdint>
+
+#include "common.cuh"
+#include "ptx.cuh"
+
+namespace aegis::umma {
+
+inline constexpr int BM = 128;
+inline constexpr int BK = 64;  // 64 16-bit elements = one 128-byte swizzle row
+inline constexpr int kThreads = 192;
+inline constexpr int kGroupM = 8;
+inline constexpr int kMaxPeers = 8;
+
+enum Epi : int { kEpiStore = 0, kEpiPartial = 1, kEpiPeers = 2 };
+
+struct Args {
+  int M, N, K;
+  int batch;
+  int a_batched, b_batched;  // use the batch coordinate for A / B loads
+  int tiles_m, tiles_n;
+  int splits, kb_per_split, kb_total;
+  long long units;  // batch * tiles_m * tiles_n * splits
+  void* C;
+  long long ldc, stride_c;
+  float alpha, beta;
+  float* partials;           // kEpiPartial: [split][batch][M][N] FP32
+  void* peers[kMaxPeers];    // kEpiPeers: every rank's C (row-major, ldc)
+  int npeers, col_offset;    // kEpiPeers: ranks; this rank's first column
+  unsigned* status;          // per-device watchdog word
+  long long wait_limit_ns;
+};
+
+template <int BN, int STAGES>
+struct Layout {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_TX = A_BYTES + B_BYTES;
+  static constexpr int A_OFF = 0;
+  static constexpr int B_OFF = STAGES * A_BYTES;
+  static constexpr int BAR_OFF = STAGES * (A_BYTES + B_BYTES);
+  static constexpr int NBARS = 2 * STAGES + 5;  // full[S], empty[S], tfull[2], tempty[2], drain
+  static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;
+  static constexpr int BYTES = MISC_OFF + 16;
+  static constexpr int ALLOC = BYTES + 1024;  // dynamic smem requested (1024-byte alignment slack)
+  static constexpr int TMEM_COLS = 2 * BN;
+  static_assert(A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "tiles must stay 1024-byte aligned");
+  static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation is a power of two");
+};
+
+struct Unit {
+  int b, m0, n0, split, kb0, nkb;
+};
+
+template <int BN>
+__device__ __forceinline__ Unit decode_unit(const Args& a, long long u) {
+  Unit r;
+  r.split = int(u % a.splits);
+  const long long tile = u / a.splits;
+  const long long per_batch = (long long)a.tiles_m * a.tiles_n;
+  r.b = int(tile / per_batch);
+  const int t = int(tile % per_batch);
+  const int span = kGroupM * a.tiles_n;
+  const int first_m = (t / span) * kGroupM;
+  const int gsize = min(a.tiles_m - first_m, kGroupM);
+  const int rr = t % span;
+  r.m0 = (first_m + rr % gsize) * BM;
+  r.n0 = (rr / gsize) * BN;
+  r.kb0 = r.split * a.kb_per_split;
+  r.nkb = min(a.kb_total - r.kb0, a.kb_per_split);
+  return r;
+}
+
+// ------------------------------------------------------------- epilogue
+template <class T>
+__device__ __forceinline__ void store_row_chunk(T* dst, const float (&v)[32], int ncols) {
+  using E = Elem<T>;
+  if (ncols == 32 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 w;
+      w.x = E::pack(v[8 * q + 0], v[8 * q + 1]);
+      w.y = E::pack(v[8 * q + 2], v[8 * q + 3]);
+      w.z = E::pack(v[8 * q + 4], v[8 * q + 5]);
+      w.w = E::pack(v[8 * q + 6], v[8 * q + 7]);
+      d4[q] = w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (i < ncols) dst[i] = E::from_f32(v[i]);
+  }
+}
+
+template <class T, int EPI>
+__device__ __forceinline__ void epilogue_chunk(const Args& a, const Unit& u, int row, int col,
+                                               const uint32_t (&r)[32]) {
+  using E = Elem<T>;
+  const int ncols = min(32, a.N - col);
+  float v[32];
+  if constexpr (EPI == kEpiPartial) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+    float* dst = a.partials + (((long long)u.split * a.batch + u.b) * a.M + row) * (long long)a.N + col;
+    if (ncols == 32 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+      float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) d4[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (i < ncols) dst[i] = v[i];
+    }
+  } else if constexpr (EPI == kEpiStore) {
+    T* dst = static_cast<T*>(a.C) + (long long)u.b * a.stride_c + (long long)row * a.ldc + col;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = a.alpha * __uint_as_float(r[i]);
+    if (a.beta != 0.f) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (i < ncols) v[i] += a.beta * E::to_f32(dst[i]);
+    }
+    store_row_chunk<T>(dst, v, ncols);
+  } else {  // kEpiPeers: plain C = A*B, the same tile into every rank's C
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+    for (int p = 0; p < a.npeers; ++p) {
+      T* dst = static_cast<T*>(a.peers[p]) + (long long)row * a.ldc + a.col_offset + col;
+      store_row_chunk<T>(dst, v, ncols);
+    }
+  }
+}
+
+// ------------------------------------------------------------- kernel
+template <class T, int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    umma_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ Args a) {
+  using L = Layout<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = ptx::smem_addr(smem);
+  const int warp = int(threadIdx.x >> 5);
+  const int lane = int(threadIdx.x & 31);
+
+  const uint32_t bar0 = sbase + L::BAR_OFF;
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
+  auto tfull_bar = [&](int acc) { return bar0 + 8u * (2 * STAGES + acc); };
+  auto tempty_bar = [&](int acc) { return bar0 + 8u * (2 * STAGES + 2 + acc); };
+  const uint32_t drain_bar = bar0 + 8u * (2 * STAGES + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::MISC_OFF);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::MISC_OFF + 4);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      ptx::mbar_init(full_bar(s), 1);
+      ptx::mbar_init(empty_bar(s), 1);
+    }
+    for (int acc = 0; acc < 2; ++acc) {
+      ptx::mbar_init(tfull_bar(acc), 1);
+      ptx::mbar_init(tempty_bar(acc), 128);
+    }
+    ptx::mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    ptx::prefetch_tensormap(&tmA);
+    ptx::prefetch_tensormap(&tmB);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(ptx::smem_addr(tmem_slot), L::TMEM_COLS);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------ TMA producer
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t filled = 0, fill_parity = 0;  // per stage: ever filled / parity of the last fill
+    for (long long unit = blockIdx.x; unit < a.units; unit += gridDim.x) {
+      const Unit u = decode_unit<BN>(a, unit);
+      const int za = a.a_batched ? u.b : 0, zb = a.b_batched ? u.b : 0;
+      bool ok = true;
+      for (int i = 0; i < u.nkb && ok; ++i) {
+        if (lane == 0)
+          ok = ptx::mbar_wait_bounded(empty_bar(stage), phase ^ 1u, abort_flag, a.status, kStatusTimeoutProducer,
+                                      a.wait_limit_ns);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        if (lane == 0) {
+          const int k0 = (u.kb0 + i) * BK;
+          const uint32_t fb = full_bar(stage);
+          ptx::mbar_arrive_expect_tx(fb, L::STAGE_TX);
+          const uint32_t sa = sbase + L::A_OFF + stage * L::A_BYTES;
+          const uint32_t sb = sbase + L::B_OFF + stage * L::B_BYTES;
+          if constexpr (A_MN) {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j) ptx::tma_load_3d(sa + j * 8192, &tmA, fb, u.m0 + 64 * j, k0, za);
+          } else {
+            ptx::tma_load_3d(sa, &tmA, fb, k0, u.m0, za);
+          }
+          if constexpr (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) ptx::tma_load_3d(sb + j * 8192, &tmB, fb, u.n0 + 64 * j, k0, zb);
+          } else {
+            ptx::tma_load_3d(sb, &tmB, fb, k0, u.n0, zb);
+          }
+          filled |= 1u << stage;
+          fill_parity = (fill_parity & ~(1u << stage)) | (phase << stage);
+        }
+        __syncwarp();
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+    }
+    // Teardown: every copy this CTA issued has landed before shared memory
+    // is released (immediate on the normal path: the MMA warp consumed them).
+    if (lane == 0) {
+      for (int s = 0; s < STAGES; ++s)
+        if (filled & (1u << s))
+          if (!ptx::mbar_wait_teardown(full_bar(s), (fill_parity >> s) & 1u, a.wait_limit_ns) && a.status)
+            atomicOr(a.status, kStatusTimeoutDrain);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc = ptx::umma_idesc_f16(Elem<T>::kBf16, A_MN, B_MN, BM, BN);
+    // Descriptor strides (bytes): SBO = 8 rows of 128 B; LBO = distance between
+    // 64-element chunks along M/N (MN-major only; 1 unit for K-major).
+    constexpr uint32_t a_lbo = A_MN ? 8192u : 16u, b_lbo = B_MN ? 8192u : 16u;
+    // Advance per K=16 step: 32 B inside the swizzled row (K-major), or 16
+    // k-rows of 128 B (MN-major).
+    constexpr uint32_t a_kstep = A_MN ? 2048u : 32u, b_kstep = B_MN ? 2048u : 32u;
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (long long unit = blockIdx.x; unit < a.units; unit += gridDim.x) {
+      const Unit u = decode_unit<BN>(a, unit);
+      bool ok = true;
+      if (lane == 0)
+        ok = ptx::mbar_wait_bounded(tempty_bar(acc), acc_phase ^ 1u, abort_flag, a.status, kStatusTimeoutMma,
+                                    a.wait_limit_ns);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      ptx::tc_fence_after();
+      const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
+      for (int i = 0; i < u.nkb && ok; ++i) {
+        if (lane == 0)
+          ok = ptx::mbar_wait_bounded(full_bar(stage), phase, abort_flag, a.status, kStatusTimeoutMma,
+                                      a.wait_limit_ns);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        ptx::tc_fence_after();
+        if (lane == 0) {
+          const uint32_t sa = sbase + L::A_OFF + stage * L::A_BYTES;
+          const uint32_t sb = sbase + L::B_OFF + stage * L::B_BYTES;
+#pragma unroll
+          for (int ks = 0; ks < BK / 16; ++ks) {
+            const uint64_t ad = ptx::sdesc_sw128(sa + ks * a_kstep, a_lbo, 1024u);
+            const uint64_t bd = ptx::sdesc_sw128(sb + ks * b_kstep, b_lbo, 1024u);
+            ptx::umma_f16(d_tmem, ad, bd, idesc, (i > 0 || ks > 0) ? 1u : 0u);
+          }
+          ptx::umma_commit(empty_bar(stage));  // frees the stage once these MMAs have read it
+        }
+        __syncwarp();
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+      if (lane == 0) ptx::umma_commit(tfull_bar(acc));  // accumulator complete
+      __syncwarp();
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  } else {
+    // ------------------------------------------------ epilogue (warps 2..5)
+    const int quarter = warp & 3;  // TMEM lanes this warp may access
+    const int row_in_tile = quarter * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (long long unit = blockIdx.x; unit < a.units; unit += gridDim.x) {
+      const Unit u = decode_unit<BN>(a, unit);
+      bool ok = true;
+      if (lane == 0)
+        ok = ptx::mbar_wait_bounded(tfull_bar(acc), acc_phase, abort_flag, a.status, kStatusTimeoutEpilogue,
+                                    a.wait_limit_ns);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      ptx::tc_fence_after();
+      const int row = u.m0 + row_in_tile;
+      const uint32_t t_row = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        ptx::tmem_ld_32x32b_x32(t_row + uint32_t(c * 32), r);
+        ptx::tmem_ld_wait(r);
+        const int col = u.n0 + c * 32;
+        if (row < a.M && col < a.N) epilogue_chunk<T, EPI>(a, u, row, col, r);
+      }
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(tempty_bar(acc));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+    if constexpr (EPI == kEpiPeers) __threadfence_system();  // peer stores complete before the kernel ends
+  }
+
+  // ------------------------------------------------ teardown
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    if (lane == 0) {
+      // Every MMA this CTA issued has finished before TMEM is released.
+      ptx::umma_commit(drain_bar);
+      if (!ptx::mbar_wait_teardown(drain_bar, 0, a.wait_limit_ns) && a.status) atomicOr(a.status, kStatusTimeoutDrain);
+    }
+    __syncwarp();
+    ptx::tmem_dealloc(tmem_base, L::TMEM_COLS);
+  }
+}
+
+}  // namespace aegis::umma

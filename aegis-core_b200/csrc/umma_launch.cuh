@@ -1,0 +1,85 @@
+#pragma once
+// Host-side launch of one umma kernel instantiation, selected at run time by
+// (BN, layouts, epilogue). Instantiated once per element type in
+// umma_f16.cu / umma_bf16.cu so the two compile in parallel.
+#include <cuda.h>
+
+#include "device.h"
+#include "umma_kernel.cuh"
+
+namespace aegis::umma {
+
+struct LaunchKey {
+  int BN, STAGES;
+  bool a_mn, b_mn;
+  int epi;
+};
+
+template <class T, int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
+cudaError_t launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const Args& a, int grid,
+                       cudaStream_t stream) {
+  auto* kern = &umma_gemm_kernel<T, BN, STAGES, A_MN, B_MN, EPI>;
+  static hw::PerDevice once;
+  constexpr size_t smem = size_t(Layout<BN, STAGES>::ALLOC);
+  if (const cudaError_t e = hw::configure_smem(once, kern, smem); e != cudaSuccess) return e;
+  kern<<<grid, kThreads, smem, stream>>>(ta, tb, a);
+  return cudaGetLastError();
+}
+
+template <class T, int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
+cudaError_t attrs_one(cudaFuncAttributes* attrs) {
+  const cudaError_t e = cudaFuncGetAttributes(attrs, &umma_gemm_kernel<T, BN, STAGES, A_MN, B_MN, EPI>);
+  if (e == cudaSuccess) attrs->sharedSizeBytes += Layout<BN, STAGES>::ALLOC;
+  return e;
+}
+
+template <class T, int BN, int STAGES, int EPI>
+cudaError_t launch_layouts(const LaunchKey& k, const CUtensorMap& ta, const CUtensorMap& tb, const Args& a,
+                           int grid, cudaStream_t s) {
+  if (!k.a_mn && k.b_mn) return launch_one<T, BN, STAGES, false, true, EPI>(ta, tb, a, grid, s);
+  if constexpr (EPI != kEpiPeers) {
+    if (!k.a_mn && !k.b_mn) return launch_one<T, BN, STAGES, false, false, EPI>(ta, tb, a, grid, s);
+    if (k.a_mn && k.b_mn) return launch_one<T, BN, STAGES, true, true, EPI>(ta, tb, a, grid, s);
+    return launch_one<T, BN, STAGES, true, false, EPI>(ta, tb, a, grid, s);
+  }
+  return cudaErrorNotSupported;
+}
+
+template <class T, int BN, int STAGES>
+cudaError_t launch_epi(const LaunchKey& k, const CUtensorMap& ta, const CUtensorMap& tb, const Args& a, int grid,
+                       cudaStream_t s) {
+  switch (k.epi) {
+    case kEpiStore: return launch_layouts<T, BN, STAGES, kEpiStore>(k, ta, tb, a, grid, s);
+    case kEpiPartial: return launch_layouts<T, BN, STAGES, kEpiPartial>(k, ta, tb, a, grid, s);
+    case kEpiPeers:
+      if constexpr (BN == 256) return launch_layouts<T, BN, STAGES, kEpiPeers>(k, ta, tb, a, grid, s);
+      return cudaErrorNotSupported;
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+// The instantiations the registry lists (gemm::UMMA_CONFIGS): (256, 4), (128, 6).
+template <class T>
+cudaError_t launch_family(const LaunchKey& k, const CUtensorMap& ta, const CUtensorMap& tb, const Args& a,
+                          int grid, cudaStream_t s) {
+  if (k.BN == 256 && k.STAGES == 4) return launch_epi<T, 256, 4>(k, ta, tb, a, grid, s);
+  if (k.BN == 128 && k.STAGES == 6) return launch_epi<T, 128, 6>(k, ta, tb, a, grid, s);
+  return cudaErrorNotSupported;
+}
+
+template <class T>
+cudaError_t attrs_family(int BN, int STAGES, cudaFuncAttributes* attrs) {
+  if (BN == 256 && STAGES == 4) return attrs_one<T, 256, 4, false, true, kEpiStore>(attrs);
+  if (BN == 128 && STAGES == 6) return attrs_one<T, 128, 6, false, true, kEpiStore>(attrs);
+  return cudaErrorNotSupported;
+}
+
+// Explicit instantiations live in umma_f16.cu and umma_bf16.cu.
+extern template cudaError_t launch_family<__half>(const LaunchKey&, const CUtensorMap&, const CUtensorMap&,
+                                                  const Args&, int, cudaStream_t);
+extern template cudaError_t launch_family<__nv_bfloat16>(const LaunchKey&, const CUtensorMap&, const CUtensorMap&,
+                                                         const Args&, int, cudaStream_t);
+extern template cudaError_t attrs_family<__half>(int, int, cudaFuncAttributes*);
+extern template cudaError_t attrs_family<__nv_bfloat16>(int, int, cudaFuncAttributes*);
+
+}  // namespace aegis::umma

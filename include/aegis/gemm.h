@@ -1,0 +1,167 @@
+#pragma once
+// aegis-b200 C++ GEMM interface: the problem description every kernel takes,
+// the kernel registry, and the per-family configuration tables.
+//
+// Mirrors the reference's include/aegis/gemm.h (Riffe007/aegis-core):
+//   GemmParams / row_major_params / validate / is_empty  (gemm.h:46-73)
+//   KernelReq / KernelEntry / DeviceCaps / registry()     (gemm.h:91-134)
+// with one addition, GemmParams::dtype (f16 or bf16; the reference is
+// f16-only), and new B200 kernel families in place of the reference's
+// sm_80/sm_90-style tiers:
+//   umma_*   tcgen05 (TMEM accumulator) + TMA + mbarrier warp-specialised GEMM,
+//            optionally with deterministic split-K (suffix _ksm);
+//   gemv_*   decode GEMV for M <= 16, 128-bit weight streaming on CUDA cores,
+//            deterministic split-K;
+//   simt_*   the general kernel: any layout, leading dimension and alignment.
+//
+// Semantics (identical to the reference): for batch b in [0, batch)
+//   C_b = alpha * A_b * B_b + beta * C_b,  FP32 accumulation,
+// A_b = A + b*stride_a (M x K), B_b = B + b*stride_b (K x N), C_b = C + b*stride_c
+// (M x N row-major, ldc >= N). alpha == 0: A*B does not contribute (NaN/Inf in
+// A or B do not propagate). beta == 0: C is not read. Empty sizes: no-op.
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <span>
+#include <string>
+#include <string_view>
+
+namespace aegis::gemm {
+
+enum class Layout : int { RowMajor = 0, ColMajor = 1 };
+enum class DType : int { F16 = 0, BF16 = 1 };
+
+struct GemmParams {
+  const void* A = nullptr;
+  const void* B = nullptr;
+  void* C = nullptr;
+  int M = 0, N = 0, K = 0;
+  Layout layout_a = Layout::RowMajor, layout_b = Layout::RowMajor;
+  long long lda = 0, ldb = 0, ldc = 0;
+  float alpha = 1.f, beta = 0.f;
+  int batch = 1;
+  long long stride_a = 0, stride_b = 0, stride_c = 0;
+  DType dtype = DType::F16;
+};
+
+// Packed row-major NN, alpha 1, beta 0, one batch (reference gemm.h:59-66).
+inline GemmParams row_major_params(const void* A, const void* B, void* C, int M, int N, int K,
+                                   DType dt = DType::F16) {
+  GemmParams p;
+  p.A = A; p.B = B; p.C = C;
+  p.M = M; p.N = N; p.K = K;
+  p.lda = K; p.ldb = N; p.ldc = N;
+  p.dtype = dt;
+  return p;
+}
+
+// cudaSuccess, or cudaErrorInvalidValue for negative sizes, null operands with
+// nonzero sizes, a bad layout/dtype, ld below the contiguous extent, negative
+// A/B batch strides or overlapping C batches (reference registry.cu:13-30).
+cudaError_t validate(const GemmParams& p);
+inline bool is_empty(const GemmParams& p) {
+  return p.M == 0 || p.N == 0 || p.K == 0 || p.batch == 0;
+}
+
+// ---------------------------------------------------------------------------
+// Registry (reference gemm.h:91-134).
+// ---------------------------------------------------------------------------
+// Legacy row-major f16 entry: C = A*B, packed (lda = K, ldb = N, ldc = N).
+using LaunchFn = cudaError_t (*)(const void* A, const void* B, void* C, int M, int N, int K,
+                                 cudaStream_t stream);
+using AttrsFn = cudaError_t (*)(cudaFuncAttributes* attrs);
+// General entry: validates p, launches asynchronously on `stream`.
+using RunFn = cudaError_t (*)(const GemmParams& p, cudaStream_t stream);
+
+struct KernelReq {
+  int min_arch = 0;       // major*10 + minor; the umma family needs exactly sm_100 (arch 100)
+  bool tma = false;       // uses cp.async.bulk.tensor
+  bool tcgen05 = false;   // uses tcgen05 / TMEM
+  size_t smem_bytes = 0;  // dynamic + static smem per block
+  int threads = 0;
+  int regs = -1;          // filled from cudaFuncGetAttributes
+};
+
+struct KernelEntry {
+  const char* name;
+  const char* config;  // JSON of the template parameters
+  LaunchFn launch;
+  AttrsFn attrs;
+  RunFn run;
+  int tune_max_m = 0;  // > 0: the tuner only times shapes with M <= this
+  KernelReq req{};
+};
+
+struct DeviceCaps {
+  int arch = 0;
+  bool tma_built = true;
+  size_t smem_per_block_optin = 0;
+  int regs_per_block = 0;
+  int max_threads_per_block = 0;
+};
+DeviceCaps current_caps();
+bool supported(const KernelEntry& e, const DeviceCaps& caps, std::string* why = nullptr);
+
+std::span<const KernelEntry> registry();
+const KernelEntry* find(std::string_view name);
+
+// ---------------------------------------------------------------------------
+// umma family: tcgen05.mma kind::f16 (f16 or bf16 operands, FP32 accumulator
+// in TMEM), cta_group::1, BM = 128 rows (TMEM lanes) x BN columns, BK = 64
+// (one 128-byte swizzle row of 16-bit elements per k-block), STAGES-deep TMA
+// ring. Persistent: one CTA per SM walks the tile list. TMEM holds two
+// accumulators, so the epilogue of a tile overlaps the main loop of the next.
+// SPLITK: 0 = never split K; 1 = split K by the SM count when the tile count
+// alone cannot fill the GPU (partials reduced in a fixed order, bit-identical
+// across runs). Name: umma_<BM>x<BN>x<BK>_s<STAGES>[_ksm].
+// ---------------------------------------------------------------------------
+struct UmmaConfig { int BM, BN, BK, STAGES, SPLITK; };
+inline constexpr UmmaConfig UMMA_CONFIGS[] = {
+    {128, 256, 64, 4, 0},
+    {128, 128, 64, 6, 0},
+    {128, 256, 64, 4, 1},
+    {128, 128, 64, 6, 1},
+};
+std::span<const KernelEntry> umma_entries();
+
+// ---------------------------------------------------------------------------
+// gemv family (decode, M <= 16 per row tile; any M runs): weights B streamed
+// with 16-byte loads, LPR lanes per B row (BN = 8*LPR columns per CTA), the
+// other threads stacked along K; FP32 FMA on CUDA cores; per-CTA fixed-order
+// tree reduction through shared memory; deterministic split-K sized by the SM
+// count. Name: gemv_<BN>x<THREADS>_ksm.
+// ---------------------------------------------------------------------------
+struct GemvConfig { int BN, THREADS; };
+inline constexpr GemvConfig GEMV_CONFIGS[] = {
+    {256, 256}, {128, 256}, {64, 256}, {32, 256},
+};
+std::span<const KernelEntry> gemv_entries();
+
+// ---------------------------------------------------------------------------
+// simt family: the general kernel (any layout, ld, alignment, batch stride).
+// Name: simt_<BM>x<BN>x<BK>.
+// ---------------------------------------------------------------------------
+std::span<const KernelEntry> simt_entries();
+
+// Split-K partials beyond this lower S (reference gemm.h:268).
+inline constexpr long long kSplitKMaxWorkspace = 256ll << 20;
+
+// The launch an umma/gemv entry makes for p on the current device (or the
+// thread's simulated one): effective splits and CTA count.
+struct LaunchPlan {
+  int splits = 1;
+  int k_chunk = 0;       // K rows per split
+  long long tiles = 0;   // output tiles (all batches)
+  unsigned grid = 0;     // CTAs launched
+};
+bool launch_plan(const char* impl, const GemmParams& p, LaunchPlan* out);
+int split_count(const char* impl, const GemmParams& p);
+
+// Whether the umma (TMA) path can address p: 16-byte aligned base pointers,
+// leading dimensions and batch strides that are multiples of 8 elements,
+// non-zero batch strides for batched operands. Otherwise umma entries run the
+// simt kernel (reference mma_tma.cu:297-305 plays the same role).
+bool tma_compatible(const GemmParams& p);
+
+}  // namespace aegis::gemm

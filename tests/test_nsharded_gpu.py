@@ -1,0 +1,54 @@
+"""N-sharded GEMM with the all-gather fused into the epilogue.
+
+On one GPU every rank is emulated in turn: rank r's call computes its column
+shard and stores it into every "rank's" C (all local buffers here, peers'
+IPC-mapped memory on a multi-GPU node). Each C must then equal the 1-GPU
+GEMM bit for bit (the per-element K order does not depend on the column
+offset). Nothing waits on anything: each emulated rank is one ordinary
+launch. The multi-process NVLink run is tests/test_nsharded_multigpu.py."""
+import numpy as np
+import pytest
+
+import aegis_capi as ac
+from gpu_util import context, dev, host
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("nranks", [1, 2, 4, 8])
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+def test_emulated_ranks_match_single_gpu_bitwise(cuda, nranks, dtype):
+    torch = cuda
+    M, N, K = 512, 2048, 1024
+    code = ac.DTYPE_BF16 if dtype == "bf16" else ac.DTYPE_F16
+    g = ac.Generator(16384)
+    A, B = g.uniform(M * K, dtype), g.uniform(K * N, dtype)
+    ctx = context(torch)
+    dA, dB = dev(torch, A), dev(torch, B)
+    full = dev(torch, np.zeros(M * N, np.uint16))
+    ctx.gemm(dA.data_ptr(), dB.data_ptr(), full.data_ptr(), M, N, K, code)
+    ctx.synchronize()
+    want = host(full)
+    ns = N // nranks
+    Bm = B.reshape(K, N)
+    shards = [dev(torch, np.ascontiguousarray(Bm[:, r * ns:(r + 1) * ns])) for r in range(nranks)]
+    cs = [dev(torch, np.full(M * N, 0x7E00, np.uint16)) for _ in range(nranks)]
+    for r in range(nranks):
+        ctx.nsharded(M, N, K, dA.data_ptr(), K, shards[r].data_ptr(), ns, [c.data_ptr() for c in cs], N, nranks, r,
+                     code)
+    ctx.synchronize()
+    for r in range(nranks):
+        assert np.array_equal(host(cs[r]), want), f"rank {r} of {nranks}"
+
+
+def test_argument_checks(cuda):
+    torch = cuda
+    ctx = context(torch)
+    buf = torch.zeros(1024, dtype=torch.int16, device="cuda")
+    p = buf.data_ptr()
+    with pytest.raises(ac.AegisError):
+        ctx.nsharded(16, 30, 16, p, 16, p, 10, [p, p, p, p], 30, 4, 0)   # N % nranks != 0
+    with pytest.raises(ac.AegisError):
+        ctx.nsharded(16, 32, 16, p, 16, p, 8, [p, p], 16, 2, 0)          # ldc < N
+    with pytest.raises(ac.AegisError):
+        ctx.nsharded(16, 32, 16, p, 16, p, 8, [p, p], 32, 2, 2)          # rank out of range
