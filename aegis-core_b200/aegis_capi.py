@@ -31,6 +31,7 @@ AEGIS_ERR_LAUNCH_FAILED = -6
 ROW_MAJOR, COL_MAJOR = 0, 1
 DTYPE_F16, DTYPE_BF16 = 0, 1
 IPC_HANDLE_BYTES = 64
+CUDA_STREAM_LEGACY = 0x1  # cudaStreamLegacy
 
 _lib = None
 _datagen_lib = None
@@ -151,7 +152,12 @@ class Context:
         self.close()
 
     def set_stream(self, stream: int | None) -> None:
-        check(self.lib.aegis_set_stream(self.ptr, c_void_p(stream or 0)), "aegis_set_stream")
+        """Queue this context's work on `stream` (a cudaStream_t as int).
+        0 is the legacy default stream (torch's default stream reports
+        handle 0): it is passed as cudaStreamLegacy, because a NULL stream in
+        the C ABI means the context's own stream. None: the context's own."""
+        handle = CUDA_STREAM_LEGACY if stream == 0 else (stream or 0)
+        check(self.lib.aegis_set_stream(self.ptr, c_void_p(handle)), "aegis_set_stream")
 
     def synchronize(self) -> None:
         check(self.lib.aegis_synchronize(self.ptr), "aegis_synchronize")

@@ -43,7 +43,7 @@ struct GemvArgs {
   const void* B;
   void* C;
   int M, N, K;
-  int ra;                    // A row-major
+  int ra, rb;                // A / B row-major
   long long lda, ldb, ldc, sa, sb, sc;
   float alpha, beta;
   int tiles_n, tiles_m;
@@ -72,7 +72,8 @@ __device__ __forceinline__ void unpack8(const uint4& v, float (&b)[8]) {
   b[4] = p2.x; b[5] = p2.y; b[6] = p3.x; b[7] = p3.y;
 }
 
-// VECB: B row-major with 16-byte-aligned rows (base, ldb); otherwise element loads.
+// VECB: B row-major with 16-byte-aligned rows (base, ldb); otherwise element loads
+// (row- or column-major B, any alignment).
 template <class T, int LPR, int MT, bool VECB>
 __global__ void __launch_bounds__(GThreads) gemv_kernel(GemvArgs a) {
   using E = Elem<T>;
@@ -136,7 +137,7 @@ __global__ void __launch_bounds__(GThreads) gemv_kernel(GemvArgs a) {
           } else {
             uint16_t h[8] = {};
             for (int j = 0; j < ncols; ++j) {
-              const T* src = B + gk + (long long)(n + j) * a.ldb;  // column-major (or misaligned) B
+              const T* src = a.rb ? B + gk * a.ldb + n + j : B + gk + (long long)(n + j) * a.ldb;
               h[j] = *reinterpret_cast<const uint16_t*>(src);
             }
             bv[u] = make_uint4(h[0] | (uint32_t(h[1]) << 16), h[2] | (uint32_t(h[3]) << 16),
@@ -334,6 +335,7 @@ cudaError_t gemv_run(int cfg, const GemmParams& p, cudaStream_t stream) {
   a.N = p.N;
   a.K = p.K;
   a.ra = p.layout_a == Layout::RowMajor;
+  a.rb = p.layout_b == Layout::RowMajor;
   a.lda = p.lda;
   a.ldb = p.ldb;
   a.ldc = p.ldc;

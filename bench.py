@@ -204,7 +204,8 @@ def bench_nshard(args, rank, local_rank, world):
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device("cuda", local_rank))
-    stream = torch.cuda.current_stream()
+    stream = torch.cuda.Stream()  # every launch, copy, event and collective of this rank on one stream
+    torch.cuda.set_stream(stream)
     ctx = ac.Context(local_rank)
     ctx.set_stream(stream.cuda_stream)
     c0, ns = ad.shard_columns(N, world, rank)
@@ -410,7 +411,8 @@ def bench_single(args):
 
     import aegis_capi as ac
     torch.cuda.set_device(0)
-    stream = torch.cuda.current_stream()
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
     ctx = ac.Context(0)
     ctx.set_stream(stream.cuda_stream)
     wl = args.workload
