@@ -80,6 +80,8 @@ _SIGNATURES = {
     "aegis_registry_json": (c_int, [c_void_p, c_char_p, c_size_t, POINTER(c_size_t)]),
     "aegis_gemm_plan_json": (c_int, [c_void_p, c_char_p, c_int, c_int, c_int, c_int, c_char_p, c_size_t,
                                      POINTER(c_size_t)]),
+    "aegis_gemv_noalloc": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_float, c_void_p, c_int64,
+                                   c_void_p, c_int64, c_float, c_void_p, c_int64]),
     "aegis_watchdog_selftest": (c_int, [c_void_p, c_int64]),
 }
 
@@ -212,6 +214,12 @@ class Context:
 
     def ipc_close_handle(self, dptr: int) -> None:
         check(self.lib.aegis_ipc_close_handle(self.ptr, c_void_p(dptr)), "aegis_ipc_close_handle")
+
+    def gemv_noalloc(self, dtype, layout_a, layout_b, M, N, K, alpha, A, lda, B, ldb, beta, C, ldc) -> None:
+        """aegis_gemv_noalloc: the decode GEMV with its scratch in the library's
+        fixed device array (no allocation on any call)."""
+        check(self.lib.aegis_gemv_noalloc(self.ptr, dtype, layout_a, layout_b, M, N, K, alpha, c_void_p(A), lda,
+                                          c_void_p(B), ldb, beta, c_void_p(C), ldc), "aegis_gemv_noalloc")
 
     def watchdog_selftest(self, timeout_ns: int) -> int:
         return self.lib.aegis_watchdog_selftest(self.ptr, timeout_ns)

@@ -404,6 +404,29 @@ int aegis_gemm_plan_json(aegis_context* ctx, const char* impl, int dtype, int M,
   return copy_out(b, buf, buf_len, needed);
 }
 
+int aegis_gemv_noalloc(aegis_context* ctx, int dtype, int layout_a, int layout_b, int M, int N, int K, float alpha,
+                       const void* A, int64_t lda, const void* B, int64_t ldb, float beta, void* C, int64_t ldc) {
+  const char* fn = "aegis_gemv_noalloc";
+  if (dtype != AEGIS_DTYPE_F16 && dtype != AEGIS_DTYPE_BF16) return fail_arg(fn, "dtype must be AEGIS_DTYPE_F16 or AEGIS_DTYPE_BF16");
+  aegis::gemm::GemmParams p;
+  if (!to_layout(layout_a, &p.layout_a) || !to_layout(layout_b, &p.layout_b))
+    return fail_arg(fn, "layout must be AEGIS_ROW_MAJOR or AEGIS_COL_MAJOR");
+  if (int s = enter(ctx, fn)) return s;
+  p.A = A; p.B = B; p.C = C;
+  p.M = M; p.N = N; p.K = K;
+  p.lda = lda; p.ldb = ldb; p.ldc = ldc;
+  p.alpha = alpha; p.beta = beta;
+  p.dtype = dtype == AEGIS_DTYPE_BF16 ? aegis::gemm::DType::BF16 : aegis::gemm::DType::F16;
+  const char* why = "";
+  const cudaError_t e = aegis::gemv_run_noalloc(p, ctx->stream, &why);
+  if (e == cudaSuccess) return AEGIS_OK;
+  cudaGetLastError();
+  if (e == cudaErrorInvalidValue)
+    return fail_arg(fn, *why ? why : "negative size, too-small leading dimension or null operand");
+  ctx->last_error = cudaGetErrorString(e);
+  return fail(AEGIS_ERR_LAUNCH_FAILED, std::string(fn) + ": " + (*why ? why : "") + " " + cudaGetErrorString(e));
+}
+
 int aegis_watchdog_selftest(aegis_context* ctx, int64_t timeout_ns) {
   if (timeout_ns < 100000 || timeout_ns > 10000000000ll)
     return fail_arg("aegis_watchdog_selftest", "timeout_ns must be in [1e5, 1e10]");

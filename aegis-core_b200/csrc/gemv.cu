@@ -20,6 +20,7 @@
 //     Nothing waits on another CTA.
 // No tensor cores: the shape is memory-bound.
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 #include "device.h"
@@ -393,6 +394,116 @@ cudaError_t gemv_attrs(int cfg, cudaFuncAttributes* attrs) {
     case 8: return cudaFuncGetAttributes(attrs, &gemv_kernel<__half, 8, 1, true>);
     default: return cudaFuncGetAttributes(attrs, &gemv_kernel<__half, 4, 1, true>);
   }
+}
+
+// --------------------------------------------------------------- allocation-free entry
+// The decode GEMV above takes its split-K tickets and partials from the
+// per-stream workspace cache, which calls cudaMalloc the first time a stream
+// needs a size class. Some callers cannot allow that: engines that hand all
+// device memory to their own allocator at start-up and forbid allocations
+// afterwards, code that runs while a CUDA graph is being captured (where
+// cudaMalloc is not allowed, and the cache refuses a first use), and
+// processes on a hard memory budget where a late allocation may fail. For
+// them, gemv_run_noalloc runs the same kernel with its scratch in the
+// fixed array below, which the CUDA module reserves on every GPU that loads
+// this library, for the life of the process.
+//
+// Capacity: kNoAllocPartialBytes of FP32 partials and kNoAllocCounterBytes of
+// tickets. A plan whose partials would not fit uses fewer splits; problems
+// beyond kNoAllocMaxM rows, kNoAllocMaxN columns or one batch are rejected.
+// Every call shares the array and leaves its contents behind: the tickets
+// are cleared on the stream before each launch; calls whose kernels overlap
+// on the GPU (several streams at once) race on the array.
+namespace {
+
+constexpr size_t kNoAllocPartialBytes = size_t(4) << 20;  // 4 MiB
+constexpr size_t kNoAllocCounterBytes = size_t(16) << 10;   // 4096 tickets
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocPartialBytes + kNoAllocCounterBytes];
+
+std::mutex g_noalloc_mu;
+unsigned char* g_noalloc_ptr[hw::kMaxCachedDevices] = {};
+
+// The device address of g_noalloc_scratch on the current device, looked up
+// once per device (with that device current). In host code the symbol itself
+// is only a host-side stand-in; it must never be passed to a kernel.
+cudaError_t noalloc_scratch(unsigned char** out) {
+  *out = nullptr;
+  int dev = 0;
+  if (const cudaError_t e = cudaGetDevice(&dev); e != cudaSuccess) return e;
+  if (dev < 0 || dev >= hw::kMaxCachedDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    if (const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch); e != cudaSuccess) return e;
+    g_noalloc_ptr[dev] = static_cast<unsigned char*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return cudaSuccess;
+}
+
+}  // namespace
+
+cudaError_t gemv_run_noalloc(const GemmParams& p, cudaStream_t stream, const char** why) {
+  *why = "";
+  if (const cudaError_t e = gemm::validate(p); e != cudaSuccess) {
+    *why = "invalid GEMM parameters";
+    return e;
+  }
+  if (gemm::is_empty(p)) return cudaSuccess;
+  if (p.batch != 1 || p.M > kNoAllocMaxM || p.N > kNoAllocMaxN) {
+    *why = "the allocation-free GEMV takes one batch, M <= 16 and N <= 65536";
+    return cudaErrorInvalidValue;
+  }
+  if (p.alpha == 0.f) return scale_c(p, stream);
+  const int cfg = p.M <= 4 ? 0 : (p.M <= 8 ? 1 : 2);  // gemv_256 / gemv_128 / gemv_64 (the dispatcher's rule)
+  GPlan pl = plan_for(cfg, p);
+  const long long slot_bytes = pl.tiles * pl.MT * (8 * pl.LPR) * (long long)sizeof(float);
+  if ((long long)pl.S * slot_bytes > (long long)kNoAllocPartialBytes) {
+    // Fewer, longer splits so the partials fit the fixed array.
+    const int s_fit = int(std::max<long long>(1, (long long)kNoAllocPartialBytes / slot_bytes));
+    pl.kc = ceil_div(ceil_div(p.K, s_fit), 16) * 16;
+    pl.S = ceil_div(p.K, pl.kc);
+    if (pl.S == 1) pl.kc = p.K;
+  }
+  if (pl.tiles * (long long)sizeof(unsigned) > (long long)kNoAllocCounterBytes) {
+    *why = "too many output tiles for the fixed ticket array";
+    return cudaErrorInvalidValue;
+  }
+  GemvArgs a{};
+  a.A = p.A;
+  a.B = p.B;
+  a.C = p.C;
+  a.M = p.M;
+  a.N = p.N;
+  a.K = p.K;
+  a.ra = p.layout_a == Layout::RowMajor;
+  a.rb = p.layout_b == Layout::RowMajor;
+  a.lda = p.lda;
+  a.ldb = p.ldb;
+  a.ldc = p.ldc;
+  a.alpha = p.alpha;
+  a.beta = p.beta;
+  a.tiles_n = pl.tiles_n;
+  a.tiles_m = pl.tiles_m;
+  a.S = pl.S;
+  a.kc = pl.kc;
+  if (pl.S > 1) {
+    unsigned char* scratch = nullptr;
+    if (const cudaError_t e = noalloc_scratch(&scratch); e != cudaSuccess) {
+      *why = "cudaGetSymbolAddress of the fixed scratch array failed";
+      return e;
+    }
+    a.partials = reinterpret_cast<float*>(scratch);
+    a.counters = reinterpret_cast<unsigned*>(scratch + kNoAllocPartialBytes);
+    // Tickets must read zero at launch (a completed launch leaves them zero;
+    // clearing here also covers a launch that never completed).
+    if (const cudaError_t e = cudaMemsetAsync(a.counters, 0, size_t(pl.tiles) * sizeof(unsigned), stream);
+        e != cudaSuccess)
+      return e;
+  }
+  const dim3 grid(unsigned((long long)pl.tiles_n * pl.S), unsigned(pl.tiles_m), 1u);
+  return p.dtype == DType::BF16 ? launch_all<__nv_bfloat16>(vec_b_ok(p), pl.LPR, pl.MT, a, grid, stream)
+                                : launch_all<__half>(vec_b_ok(p), pl.LPR, pl.MT, a, grid, stream);
 }
 
 }  // namespace aegis

@@ -34,6 +34,14 @@ cudaError_t gemv_run(int cfg, const gemm::GemmParams& p, cudaStream_t stream);
 gemm::LaunchPlan gemv_plan(int cfg, const gemm::GemmParams& p);
 cudaError_t gemv_attrs(int cfg, cudaFuncAttributes* attrs);
 
+// Allocation-free decode GEMV: the gemv kernel with its split-K scratch in
+// a fixed device array of this library (no cudaMalloc, cudaFree or other
+// allocation on any call). One batch, M <= kNoAllocMaxM, N <= kNoAllocMaxN;
+// *why names the reason of a rejection.
+inline constexpr int kNoAllocMaxM = 16;
+inline constexpr int kNoAllocMaxN = 65536;
+cudaError_t gemv_run_noalloc(const gemm::GemmParams& p, cudaStream_t stream, const char** why);
+
 // Watchdog self-test kernel: one wait that nothing completes.
 cudaError_t watchdog_selftest(long long limit_ns, cudaStream_t stream, unsigned* bits_out);
 

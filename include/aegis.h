@@ -255,6 +255,29 @@ AEGIS_API int aegis_registry_json(aegis_context* ctx, char* buf, size_t buf_len,
 AEGIS_API int aegis_gemm_plan_json(aegis_context* ctx, const char* impl, int dtype, int M, int N, int K, char* buf,
                                    size_t buf_len, size_t* needed);
 
+/* ---- ABI 1.4 addition: decode GEMV that allocates nothing -------------------
+ * C = alpha * A * B + beta * C for decode shapes, like aegis_gemm_*_ex with
+ * row- or column-major A and B (layout_a, layout_b), one batch, M <= 16 and
+ * N <= 65536; dtype AEGIS_DTYPE_F16 or AEGIS_DTYPE_BF16. Larger problems:
+ * AEGIS_ERR_INVALID_ARGUMENT with the reason in aegis_last_error_string().
+ * The regular entry points take their split-K scratch from a per-stream cache
+ * that calls cudaMalloc the first time a stream needs it. This one is for
+ * callers that cannot allow that: engines that give all device memory to
+ * their own allocator at start-up and forbid later allocations, code that
+ * runs while a CUDA graph is being captured, and processes on a hard memory
+ * budget. It calls no cudaMalloc, cudaFree or other allocating routine: its
+ * scratch is a fixed 4 MiB + 16 KiB array inside this library, which every
+ * GPU that loads the library holds until the process exits (a plan that
+ * would need more uses fewer K splits). The first call on a device looks up
+ * that array's device address, so make it before any stream capture. Every
+ * call shares the array: calls whose kernels overlap on the GPU (concurrent
+ * streams) race and must be serialised by the caller. Same kernel and
+ * results as the dispatcher's GEMV for these shapes (deterministic split-K).
+ * No counterpart in the reference, which has no allocation-free path. */
+AEGIS_API int aegis_gemv_noalloc(aegis_context* ctx, int dtype, int layout_a, int layout_b, int M, int N, int K,
+                                 float alpha, const void* A, int64_t lda, const void* B, int64_t ldb, float beta,
+                                 void* C, int64_t ldc);
+
 /* ---- ABI 1.4 addition: watchdog self-test ----------------------------------
  * Every wait inside this library's kernels is bounded. This runs one small
  * kernel whose wait can never complete, with the given limit (1e5..1e10 ns),
