@@ -8,8 +8,8 @@
 //     elements each), so a warp reads 32/LPR rows x BN*2 contiguous bytes per
 //     load instruction; the RG = 256/LPR row groups stride down the slice.
 //     U independent 16-byte loads per thread are in flight before any math.
-//   - A's slice rows are staged in shared memory as FP32 [k][MT] (chunks of
-//     KCH rows), read as broadcasts.
+//   - A's rows for a batch are staged in shared memory as FP32 [k][MT] while
+//     the batch's weight loads are in flight, and read as broadcasts.
 //   - FP32 FMA into MT x 8 accumulators per thread, k ascending.
 //   - Reduction: row groups inside a warp by a fixed shuffle-xor tree, then
 //     the 8 warps through shared memory in warp order 0..7.
@@ -37,7 +37,12 @@ namespace {
 
 constexpr int GThreads = 256;
 constexpr int kSmemFloats = 8192;  // 32 KiB: A chunk, then the cross-warp reduction (aliased)
-constexpr int kMinSplitRows = 128;
+
+// Rows per thread per batch (= independent 16-byte weight loads in flight):
+// bounded by the registers the MT x 8 accumulators leave.
+__host__ __device__ constexpr int gemv_rows_per_thread(int MT) {
+  return MT <= 2 ? 16 : (MT == 4 ? 8 : (MT == 8 ? 4 : 2));
+}
 
 struct GemvArgs {
   const void* A;
@@ -80,9 +85,9 @@ __global__ void __launch_bounds__(GThreads) gemv_kernel(GemvArgs a) {
   using E = Elem<T>;
   constexpr int BN = 8 * LPR;
   constexpr int RG = GThreads / LPR;
-  constexpr int KCH = kSmemFloats / MT;                  // A rows staged per chunk
-  constexpr int U = MT >= 8 ? 2 : (MT >= 4 ? 4 : 8);     // loads in flight per thread
+  constexpr int U = gemv_rows_per_thread(MT);            // 16-byte loads in flight per thread
   static_assert(8 * MT * BN <= kSmemFloats, "cross-warp reduction must fit the shared buffer");
+  static_assert(RG * U * MT <= kSmemFloats, "a batch of A rows must fit the shared buffer");
   __shared__ __align__(16) float sm[kSmemFloats];
   __shared__ int s_last;
 
@@ -106,54 +111,55 @@ __global__ void __launch_bounds__(GThreads) gemv_kernel(GemvArgs a) {
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[m][j] = 0.f;
 
-  for (int c0 = k_begin; c0 < k_end; c0 += KCH) {
-    const int clen = min(KCH, k_end - c0);
-    __syncthreads();  // previous chunk fully consumed
-    for (int i = tid; i < clen * MT; i += GThreads) {
+  // Batches of U rows per thread (RG*U rows per CTA). All U weight loads of a
+  // batch are issued first; A's rows for the batch are staged into shared
+  // memory while they are in flight. The planner sizes a split to one batch.
+  for (int base = k_begin; base < k_end; base += RG * U) {
+    uint4 bv[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int k = base + g + u * RG;
+      bv[u] = make_uint4(0u, 0u, 0u, 0u);
+      if (k < k_end && ncols > 0) {
+        const long long gk = k;
+        if constexpr (VECB) {
+          const T* src = B + gk * a.ldb + n;
+          if (ncols == 8) {
+            bv[u] = __ldg(reinterpret_cast<const uint4*>(src));
+          } else {
+            uint16_t h[8] = {};
+            for (int j = 0; j < ncols; ++j) h[j] = reinterpret_cast<const uint16_t*>(src)[j];
+            bv[u] = make_uint4(h[0] | (uint32_t(h[1]) << 16), h[2] | (uint32_t(h[3]) << 16),
+                               h[4] | (uint32_t(h[5]) << 16), h[6] | (uint32_t(h[7]) << 16));
+          }
+        } else {
+          uint16_t h[8] = {};
+          for (int j = 0; j < ncols; ++j) {
+            const T* src = a.rb ? B + gk * a.ldb + n + j : B + gk + (long long)(n + j) * a.ldb;
+            h[j] = *reinterpret_cast<const uint16_t*>(src);
+          }
+          bv[u] = make_uint4(h[0] | (uint32_t(h[1]) << 16), h[2] | (uint32_t(h[3]) << 16),
+                             h[4] | (uint32_t(h[5]) << 16), h[6] | (uint32_t(h[7]) << 16));
+        }
+      }
+    }
+    const int blen = min(RG * U, k_end - base);
+    __syncthreads();  // the previous batch's A rows are consumed
+    for (int i = tid; i < blen * MT; i += GThreads) {
       const int kk = i / MT, m = i % MT;
-      const int gm = m0 + m, gk = c0 + kk;
+      const int gm = m0 + m, gk = base + kk;
       float v = 0.f;
       if (gm < a.M) v = E::to_f32(a.ra ? A[(long long)gm * a.lda + gk] : A[gm + (long long)gk * a.lda]);
       sm[kk * MT + m] = v;
     }
     __syncthreads();
-    for (int kk = g; kk < clen; kk += RG * U) {
-      uint4 bv[U];
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int k = kk + u * RG;
-        bv[u] = make_uint4(0u, 0u, 0u, 0u);
-        if (k < clen && ncols > 0) {
-          const long long gk = c0 + k;
-          if constexpr (VECB) {
-            const T* src = B + gk * a.ldb + n;
-            if (ncols == 8) {
-              bv[u] = __ldg(reinterpret_cast<const uint4*>(src));
-            } else {
-              uint16_t h[8] = {};
-              for (int j = 0; j < ncols; ++j) h[j] = reinterpret_cast<const uint16_t*>(src)[j];
-              bv[u] = make_uint4(h[0] | (uint32_t(h[1]) << 16), h[2] | (uint32_t(h[3]) << 16),
-                                 h[4] | (uint32_t(h[5]) << 16), h[6] | (uint32_t(h[7]) << 16));
-            }
-          } else {
-            uint16_t h[8] = {};
-            for (int j = 0; j < ncols; ++j) {
-              const T* src = a.rb ? B + gk * a.ldb + n + j : B + gk + (long long)(n + j) * a.ldb;
-              h[j] = *reinterpret_cast<const uint16_t*>(src);
-            }
-            bv[u] = make_uint4(h[0] | (uint32_t(h[1]) << 16), h[2] | (uint32_t(h[3]) << 16),
-                               h[4] | (uint32_t(h[5]) << 16), h[6] | (uint32_t(h[7]) << 16));
-          }
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int k = kk + u * RG;
-        if (k < clen) {
-          float bf[8];
-          unpack8<T>(bv[u], bf);
-          fma8<MT>(acc, bf, &sm[k * MT]);
-        }
+    for (int u = 0; u < U; ++u) {
+      const int kk = g + u * RG;
+      if (kk < blen) {
+        float bf[8];
+        unpack8<T>(bv[u], bf);
+        fma8<MT>(acc, bf, &sm[kk * MT]);
       }
     }
   }
@@ -256,20 +262,23 @@ GPlan plan_for(int cfg, const GemmParams& p) {
   pl.tiles = (long long)pl.tiles_n * pl.tiles_m * p.batch;
   const hw::DeviceLimits* d = hw::current();
   const int sms = d ? d->sm_count : 0;
-  // Enough CTAs for ~4 resident per SM (bytes in flight), splits at least
-  // kMinSplitRows long, partials bounded by the workspace cap.
-  int S = 1;
-  if (sms > 0) {
-    const long long target = (long long)sms * 4;
-    const long long want = (target + pl.tiles - 1) / pl.tiles;
-    const long long smax = std::max(1, p.K / kMinSplitRows);
-    const long long cap = std::max<long long>(
-        1, gemm::kSplitKMaxWorkspace / std::max<long long>(1, pl.tiles * pl.MT * c.BN * (long long)sizeof(float)));
-    S = int(std::max<long long>(1, std::min({want, smax, cap})));
+  // One batch per thread per split: kc = RG * U rows (a split's weights are
+  // all in flight at once); the partials stay within the workspace cap.
+  const int RG = 256 / pl.LPR;
+  int kc = RG * gemv_rows_per_thread(pl.MT);
+  const long long slot = pl.tiles * pl.MT * c.BN * (long long)sizeof(float);
+  const long long cap = std::max<long long>(1, gemm::kSplitKMaxWorkspace / std::max<long long>(1, slot));
+  int S = ceil_div(p.K, kc);
+  if (S > cap) {
+    S = int(cap);
+    kc = ceil_div(ceil_div(p.K, S), 16) * 16;
+    S = ceil_div(p.K, kc);
   }
-  int kc = ceil_div(ceil_div(p.K, S), 16) * 16;
-  S = ceil_div(p.K, kc);
-  if (S == 1) kc = p.K;
+  if (S <= 1) {
+    S = 1;
+    kc = p.K;
+  }
+  (void)hw::current();
   pl.S = S;
   pl.kc = kc;
   return pl;
