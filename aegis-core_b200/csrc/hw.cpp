@@ -93,7 +93,7 @@ aegis_hw_gpu_info gpu_info(int device) {
   if (cudaDeviceGetAttribute(&khz, cudaDevAttrMemoryClockRate, device) == cudaSuccess && khz > 0)
     r.max_mem_clock_mhz = khz / 1000;
   cudaGetLastError();
-  std::snprintf(r.name, sizeof r.name, "%s", p.name);
+  std::snprintf(r.name, sizeof r.name, "%.127s", p.name);
   return r;
 }
 

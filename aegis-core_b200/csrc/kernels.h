@@ -34,6 +34,14 @@ cudaError_t gemv_run(int cfg, const gemm::GemmParams& p, cudaStream_t stream);
 gemm::LaunchPlan gemv_plan(int cfg, const gemm::GemmParams& p);
 cudaError_t gemv_attrs(int cfg, cudaFuncAttributes* attrs);
 
+// ummav family: decode GEMM on tensor cores (swap-AB, stream-K segments).
+// Runs the CUDA-core gemv for problems it cannot take (ummav_applicable).
+bool ummav_applicable(const gemm::GemmParams& p);
+cudaError_t ummav_run(int cfg, const gemm::GemmParams& p, cudaStream_t stream);
+gemm::LaunchPlan ummav_plan(int cfg, const gemm::GemmParams& p);
+cudaError_t ummav_attrs(int cfg, cudaFuncAttributes* attrs);
+size_t ummav_smem_bytes(int cfg);
+
 // Allocation-free decode GEMV: the gemv kernel with its split-K scratch in
 // a fixed device array of this library (no cudaMalloc, cudaFree or other
 // allocation on any call). One batch, M <= kNoAllocMaxM, N <= kNoAllocMaxN;

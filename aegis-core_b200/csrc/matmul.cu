@@ -60,9 +60,12 @@ const gemm::KernelEntry* by_name(const char* name) {
 namespace detail {
 
 const gemm::KernelEntry* rule_for(const gemm::GemmParams& p, const gemm::DeviceCaps& caps) {
-  (void)caps;
   if (p.M <= 16) {
-    if (p.M <= 4) return by_name("gemv_256x256_ksm");
+    // Decode: the tensor-core stream (ummav) measured faster than the CUDA-core
+    // GEMV at every BASELINE decode shape; it takes row-major operands the TMA
+    // path can address, the CUDA-core GEMV everything else.
+    if (caps.arch == 100 && ummav_applicable(p)) return by_name("ummav_128x16x64_s6x2");
+    if (p.M <= 4) return by_name("gemv_128x256_ksm");
     if (p.M <= 8) return by_name("gemv_128x256_ksm");
     return by_name("gemv_64x256_ksm");
   }

@@ -140,6 +140,42 @@ const std::vector<KernelEntry>& gemv_vec() {
   return v;
 }
 
+template <int I>
+cudaError_t ummav_run_i(const GemmParams& p, cudaStream_t s) { return ummav_run(I, p, s); }
+template <int I>
+cudaError_t ummav_attrs_i(cudaFuncAttributes* a) { return ummav_attrs(I, a); }
+template <int I>
+cudaError_t ummav_launch_i(const void* A, const void* B, void* C, int M, int N, int K, cudaStream_t s) {
+  return ummav_run(I, row_major_params(A, B, C, M, N, K), s);
+}
+
+const std::vector<KernelEntry>& ummav_vec() {
+  static const std::vector<KernelEntry> v = [] {
+    static_assert(sizeof(UMMAV_CONFIGS) / sizeof(UMMAV_CONFIGS[0]) == 2, "ummav table below lists every row");
+    const RunFn runs[] = {&ummav_run_i<0>, &ummav_run_i<1>};
+    const AttrsFn attrs[] = {&ummav_attrs_i<0>, &ummav_attrs_i<1>};
+    const LaunchFn launches[] = {&ummav_launch_i<0>, &ummav_launch_i<1>};
+    std::vector<KernelEntry> out;
+    for (int i = 0; i < 2; ++i) {
+      const UmmavConfig& c = UMMAV_CONFIGS[i];
+      KernelReq req;
+      req.min_arch = 100;
+      req.tma = true;
+      req.tcgen05 = true;
+      req.smem_bytes = ummav_smem_bytes(i);
+      req.threads = 192;
+      const std::string name = "ummav_128x16x64_s" + std::to_string(c.STAGES) +
+                               (c.CTAS_PER_SM > 1 ? "x" + std::to_string(c.CTAS_PER_SM) : std::string());
+      const std::string cfg = std::string("{\"family\":\"ummav\",\"bm\":128,\"bn\":16,\"bk\":64,\"stages\":") +
+                              std::to_string(c.STAGES) + ",\"cta_group\":1,\"ctas_per_sm\":" +
+                              std::to_string(c.CTAS_PER_SM) + ",\"split\":\"stream-k\"}";
+      out.push_back({keep(name), keep(cfg), launches[i], attrs[i], runs[i], 16, req});
+    }
+    return out;
+  }();
+  return v;
+}
+
 const std::vector<KernelEntry>& simt_vec() {
   static const std::vector<KernelEntry> v = [] {
     KernelReq req;
@@ -157,11 +193,13 @@ const std::vector<KernelEntry>& simt_vec() {
 std::span<const KernelEntry> umma_entries() { return umma_vec(); }
 std::span<const KernelEntry> gemv_entries() { return gemv_vec(); }
 std::span<const KernelEntry> simt_entries() { return simt_vec(); }
+std::span<const KernelEntry> ummav_entries() { return ummav_vec(); }
 
 std::span<const KernelEntry> registry() {
   static const std::vector<KernelEntry> all = [] {
     std::vector<KernelEntry> v;
-    for (auto fam : {umma_entries(), gemv_entries(), simt_entries()}) v.insert(v.end(), fam.begin(), fam.end());
+    for (auto fam : {umma_entries(), gemv_entries(), ummav_entries(), simt_entries()})
+      v.insert(v.end(), fam.begin(), fam.end());
     // Registers (and static smem) from the compiled binary where a device answers.
     for (KernelEntry& e : v) {
       cudaFuncAttributes a{};
@@ -222,6 +260,9 @@ bool launch_plan(const char* impl, const GemmParams& p, LaunchPlan* out) {
   const auto gv = gemv_entries();
   for (size_t i = 0; i < gv.size(); ++i)
     if (name == gv[i].name) return *out = gemv_plan(int(i), p), true;
+  const auto uv = ummav_entries();
+  for (size_t i = 0; i < uv.size(); ++i)
+    if (name == uv[i].name) return *out = ummav_plan(int(i), p), true;
   return false;
 }
 

@@ -9,8 +9,6 @@
 // ordered ticket in the last CTA of each tile (src/gemm/splitk.cuh:155-222);
 // with 128x256 tiles and up to ~74 splits the last CTA would read megabytes
 // alone, so here every SM shares the (L2-resident) reduction.
-#include <cudaTypedefs.h>
-
 #include <algorithm>
 #include <cmath>
 #include <cstring>
@@ -21,6 +19,7 @@
 #include "kernels.h"
 #include "status.h"
 #include "umma_launch.cuh"
+#include "tma_map.h"
 #include "workspace.h"
 
 namespace aegis {
@@ -53,43 +52,6 @@ int splitk_choose(long long tiles, int k_blocks, int sms, int min_blocks_per_spl
 }
 
 namespace {
-
-// ---------------------------------------------------------------- tensor maps
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q{};
-    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess) {
-      cudaGetLastError();
-      p = nullptr;
-    }
-    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }();
-  return fn;
-}
-
-// A 3-D (inner, outer, batch) 16-bit tensor, 128-byte swizzled boxes of
-// {64, box_outer, 1}. ld and batch stride in elements.
-bool encode_map(CUtensorMap* map, DType dt, const void* base, long long inner, long long outer, long long ld,
-                long long batch, long long bstride, int box_outer) {
-  auto fn = encode_fn();
-  if (!fn) return false;
-  if (batch <= 1) {
-    batch = 1;
-    bstride = ((outer * ld + 7) / 8) * 8;  // unused coordinate; any legal stride
-  }
-  cuuint64_t dims[3] = {cuuint64_t(inner), cuuint64_t(outer), cuuint64_t(batch)};
-  cuuint64_t strides[2] = {cuuint64_t(ld) * 2, cuuint64_t(bstride) * 2};
-  cuuint32_t box[3] = {64, cuuint32_t(box_outer), 1};
-  cuuint32_t estr[3] = {1, 1, 1};
-  const CUtensorMapDataType t =
-      dt == DType::BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  const CUresult r = fn(map, t, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
-}
 
 struct Maps {
   CUtensorMap a, b;

@@ -271,8 +271,9 @@ AEGIS_API int aegis_gemm_plan_json(aegis_context* ctx, const char* impl, int dty
  * would need more uses fewer K splits). The first call on a device looks up
  * that array's device address, so make it before any stream capture. Every
  * call shares the array: calls whose kernels overlap on the GPU (concurrent
- * streams) race and must be serialised by the caller. Same kernel and
- * results as the dispatcher's GEMV for these shapes (deterministic split-K).
+ * streams) race and must be serialised by the caller. It runs the CUDA-core
+ * gemv kernel (deterministic split-K); results match the regular entry points
+ * within the library's tolerance.
  * No counterpart in the reference, which has no allocation-free path. */
 AEGIS_API int aegis_gemv_noalloc(aegis_context* ctx, int dtype, int layout_a, int layout_b, int M, int N, int K,
                                  float alpha, const void* A, int64_t lda, const void* B, int64_t ldb, float beta,

@@ -139,6 +139,21 @@ inline constexpr GemvConfig GEMV_CONFIGS[] = {
 std::span<const KernelEntry> gemv_entries();
 
 // ---------------------------------------------------------------------------
+// ummav family (decode, M <= 16, row-major operands the TMA path can address;
+// anything else runs the gemv family): C^T = B^T * A^T on tensor cores, the
+// weights as the 128-row tcgen05 operand and the activation rows padded to 16,
+// a STAGES-deep TMA ring, CTAS_PER_SM CTAs per SM, an even k-block split over
+// all CTAs (stream-K segments) with an ordered ticket fix-up. Deterministic.
+// Name: ummav_128x16x64_s<STAGES>[x<CTAS_PER_SM>].
+// ---------------------------------------------------------------------------
+struct UmmavConfig { int STAGES, CTAS_PER_SM; };
+inline constexpr UmmavConfig UMMAV_CONFIGS[] = {
+    {11, 1},
+    {6, 2},
+};
+std::span<const KernelEntry> ummav_entries();
+
+// ---------------------------------------------------------------------------
 // simt family: the general kernel (any layout, ld, alignment, batch stride).
 // Name: simt_<BM>x<BN>x<BK>.
 // ---------------------------------------------------------------------------

@@ -20,7 +20,8 @@ from gpu_util import check, context, dev, host, run
 pytestmark = pytest.mark.gpu
 
 IMPLS = ["umma_128x256x64_s4", "umma_128x128x64_s6", "umma_128x256x64_s4_ksm", "umma_128x128x64_s6_ksm",
-         "gemv_256x256_ksm", "gemv_128x256_ksm", "gemv_64x256_ksm", "gemv_32x256_ksm", "simt_64x64x16"]
+         "gemv_256x256_ksm", "gemv_128x256_ksm", "gemv_64x256_ksm", "gemv_32x256_ksm", "ummav_128x16x64_s11", "ummav_128x16x64_s6x2",
+         "simt_64x64x16"]
 
 
 def test_registry_all_supported(cuda):

@@ -14,7 +14,7 @@ from gpu_util import check, context, dev, host, run
 
 pytestmark = pytest.mark.gpu
 
-GEMV = ["gemv_256x256_ksm", "gemv_128x256_ksm", "gemv_64x256_ksm", "gemv_32x256_ksm"]
+GEMV = ["gemv_256x256_ksm", "gemv_128x256_ksm", "gemv_64x256_ksm", "gemv_32x256_ksm", "ummav_128x16x64_s11", "ummav_128x16x64_s6x2"]
 SHAPES = [(4096, 4096), (4096, 14336), (14336, 4096)]
 
 
@@ -31,7 +31,7 @@ def test_config3(cuda, M, K, N):
     d = op.make_desc(M, N, K)
     ref = op.gemm_ref(d, A, B)
     ctx = context(torch)
-    assert ctx.choice(M, N, K).startswith("gemv_")
+    assert ctx.choice(M, N, K).startswith(("ummav_", "gemv_"))
     dA, dB = dev(torch, A), dev(torch, B)
     for impl in [None] + GEMV:
         outs = []
