@@ -4,5 +4,5 @@
 namespace aegis::umma {
 template cudaError_t launch_family<__half>(const LaunchKey&, const CUtensorMap&, const CUtensorMap&, const Args&,
                                            int, cudaStream_t);
-template cudaError_t attrs_family<__half>(int, int, cudaFuncAttributes*);
+template cudaError_t attrs_family<__half>(int, int, bool, cudaFuncAttributes*);
 }  // namespace aegis::umma

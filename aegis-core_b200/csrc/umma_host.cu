@@ -59,14 +59,15 @@ struct Maps {
 
 // A: row-major -> K-major box {64 k, 128 m}; col-major -> M-major boxes {64 m, 64 k}.
 // B: row-major -> N-major boxes {64 n, 64 k}; col-major -> K-major box {64 k, BN n}.
-bool make_maps(const GemmParams& p, int BN, Maps* m) {
+// `bbox`: the B box width along N for K-major B (BN, or BN/2 for CTA pairs).
+bool make_maps(const GemmParams& p, int bbox, Maps* m) {
   const bool ar = p.layout_a == Layout::RowMajor, br = p.layout_b == Layout::RowMajor;
   const long long ba = p.batch > 1 && p.stride_a != 0 ? p.batch : 1;
   const long long bb = p.batch > 1 && p.stride_b != 0 ? p.batch : 1;
   const bool okA = ar ? encode_map(&m->a, p.dtype, p.A, p.K, p.M, p.lda, ba, p.stride_a, umma::BM)
                       : encode_map(&m->a, p.dtype, p.A, p.M, p.K, p.lda, ba, p.stride_a, umma::BK);
   const bool okB = br ? encode_map(&m->b, p.dtype, p.B, p.N, p.K, p.ldb, bb, p.stride_b, umma::BK)
-                      : encode_map(&m->b, p.dtype, p.B, p.K, p.N, p.ldb, bb, p.stride_b, BN);
+                      : encode_map(&m->b, p.dtype, p.B, p.K, p.N, p.ldb, bb, p.stride_b, bbox);
   return okA && okB;
 }
 
@@ -135,24 +136,63 @@ cudaError_t launch_reduce(const float* part, int S, const GemmParams& p, cudaStr
 
 // ---------------------------------------------------------------- planning
 struct Plan {
-  int BN = 256, STAGES = 4;
+  int BM = 128, BN = 256, STAGES = 4, CTAS = 1;
   int splits = 1, kb_per_split = 0, kb_total = 0;
   int tiles_m = 0, tiles_n = 0;
   long long tiles = 0, units = 0;
   int grid = 0;
 };
 
+// CTA pairs that can be resident at once on the current device (both CTAs of
+// a cluster must sit in one GPC), queried once per device; sms/2 if the query
+// is unavailable (sizing tests on a simulated device).
+int pair_slots(int sms) {
+  static std::mutex mu;
+  static int cached[hw::kMaxCachedDevices] = {};
+  const hw::DeviceLimits* d = hw::current();
+  if (!d || d->simulated) return sms;
+  int dev = d->device;
+  if (dev < 0 || dev >= hw::kMaxCachedDevices) return sms;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cached[dev] == 0) {
+    int n = 0;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(unsigned(2 * sms));
+    cfg.blockDim = dim3(umma::kThreads);
+    cfg.dynamicSmemBytes = umma::LayoutPair<256, 6>::ALLOC;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    auto* kern = &umma::umma2_gemm_kernel<__nv_bfloat16, 256, 6, false, true, umma::kEpiStore>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             int(umma::LayoutPair<256, 6>::ALLOC)) != cudaSuccess ||
+        cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = sms;
+    }
+    cached[dev] = std::min(n, sms);
+  }
+  return cached[dev];
+}
+
 Plan make_plan(int cfg, const GemmParams& p) {
   const gemm::UmmaConfig& c = gemm::UMMA_CONFIGS[cfg];
   Plan pl;
+  pl.BM = c.BM;
   pl.BN = c.BN;
   pl.STAGES = c.STAGES;
-  pl.tiles_m = ceil_div(p.M, umma::BM);
+  pl.CTAS = c.CTAS;
+  pl.tiles_m = ceil_div(p.M, c.BM);
   pl.tiles_n = ceil_div(p.N, c.BN);
   pl.kb_total = ceil_div(p.K, umma::BK);
   pl.tiles = (long long)p.batch * pl.tiles_m * pl.tiles_n;
   const hw::DeviceLimits* d = hw::current();
-  const int sms = d ? d->sm_count : 0;
+  // Tile slots: one per SM, or one per resident pair of SMs for cta_group::2.
+  const int sms = d ? (c.CTAS == 2 ? pair_slots(d->sm_count / 2) : d->sm_count) : 0;
   int S = 1;
   if (c.SPLITK && sms > 0 && pl.tiles < sms) {
     // One k-block is BK/16 = 4 MMAs of 128 x BN x 16 (about 128 cycles each at
@@ -168,7 +208,7 @@ Plan make_plan(int cfg, const GemmParams& p) {
   pl.splits = ceil_div(pl.kb_total, pl.kb_per_split);
   pl.units = pl.tiles * pl.splits;
   const long long g = sms > 0 ? std::min<long long>(pl.units, sms) : pl.units;
-  pl.grid = int(std::max<long long>(1, g));
+  pl.grid = int(std::max<long long>(1, g)) * c.CTAS;  // CTAs (pairs: two per tile slot)
   return pl;
 }
 
@@ -215,11 +255,11 @@ cudaError_t umma_run(int cfg, const GemmParams& p, cudaStream_t stream) {
   if (!gemm::tma_compatible(p) || !device_is_sm100()) return simt_run(p, stream);
   const Plan pl = make_plan(cfg, p);
   Maps maps;
-  if (!make_maps(p, pl.BN, &maps)) return simt_run(p, stream);  // TMA refused the operand geometry
+  if (!make_maps(p, pl.CTAS == 2 ? pl.BN / 2 : pl.BN, &maps)) return simt_run(p, stream);  // TMA refused the geometry
   umma::Args a = make_args(p, pl);
   if (const cudaError_t e = status::word(&a.status); e != cudaSuccess) return e;
   umma::LaunchKey k{pl.BN, pl.STAGES, p.layout_a == Layout::ColMajor, p.layout_b == Layout::RowMajor,
-                    umma::kEpiStore};
+                    umma::kEpiStore, pl.CTAS == 2};
   if (pl.splits == 1) return launch(p, k, maps, a, pl.grid, stream);
   // Split-K: partials, then the ordered reduction.
   void* part = nullptr;
@@ -244,11 +284,12 @@ gemm::LaunchPlan umma_plan(int cfg, const GemmParams& p) {
 
 cudaError_t umma_attrs(int cfg, cudaFuncAttributes* attrs) {
   const gemm::UmmaConfig& c = gemm::UMMA_CONFIGS[cfg];
-  return umma::attrs_family<__half>(c.BN, c.STAGES, attrs);
+  return umma::attrs_family<__half>(c.BN, c.STAGES, c.CTAS == 2, attrs);
 }
 
 size_t umma_smem_bytes(int cfg) {
   const gemm::UmmaConfig& c = gemm::UMMA_CONFIGS[cfg];
+  if (c.CTAS == 2) return size_t(umma::LayoutPair<256, 6>::ALLOC);
   return c.BN == 256 ? size_t(umma::Layout<256, 4>::ALLOC) : size_t(umma::Layout<128, 6>::ALLOC);
 }
 

@@ -5,7 +5,7 @@
 #include <cuda.h>
 
 #include "device.h"
-#include "umma_kernel.cuh"
+#include "umma2_kernel.cuh"
 
 namespace aegis::umma {
 
@@ -13,6 +13,7 @@ struct LaunchKey {
   int BN, STAGES;
   bool a_mn, b_mn;
   int epi;
+  bool pair = false;  // cta_group::2 kernel, clusters of two CTAs
 };
 
 template <class T, int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
@@ -27,48 +28,86 @@ cudaError_t launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const Args&
 }
 
 template <class T, int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
+cudaError_t launch_one_pair(const CUtensorMap& ta, const CUtensorMap& tb, const Args& a, int grid,
+                            cudaStream_t stream) {
+  auto* kern = &umma2_gemm_kernel<T, BN, STAGES, A_MN, B_MN, EPI>;
+  static hw::PerDevice once;
+  constexpr size_t smem = size_t(LayoutPair<BN, STAGES>::ALLOC);
+  if (const cudaError_t e = hw::configure_smem(once, kern, smem); e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(unsigned(grid));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, ta, tb, a);
+}
+
+template <class T, int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
 cudaError_t attrs_one(cudaFuncAttributes* attrs) {
   const cudaError_t e = cudaFuncGetAttributes(attrs, &umma_gemm_kernel<T, BN, STAGES, A_MN, B_MN, EPI>);
   if (e == cudaSuccess) attrs->sharedSizeBytes += Layout<BN, STAGES>::ALLOC;
   return e;
 }
 
-template <class T, int BN, int STAGES, int EPI>
+template <class T, int BN, int STAGES, int EPI, bool PAIR>
 cudaError_t launch_layouts(const LaunchKey& k, const CUtensorMap& ta, const CUtensorMap& tb, const Args& a,
                            int grid, cudaStream_t s) {
-  if (!k.a_mn && k.b_mn) return launch_one<T, BN, STAGES, false, true, EPI>(ta, tb, a, grid, s);
+#define AEGIS_UMMA_LAUNCH(AM, BMJ)                                                        \
+  [&] {                                                                                   \
+    if constexpr (PAIR) return launch_one_pair<T, BN, STAGES, AM, BMJ, EPI>(ta, tb, a, grid, s); \
+    else return launch_one<T, BN, STAGES, AM, BMJ, EPI>(ta, tb, a, grid, s);              \
+  }()
+  if (!k.a_mn && k.b_mn) return AEGIS_UMMA_LAUNCH(false, true);
   if constexpr (EPI != kEpiPeers) {
-    if (!k.a_mn && !k.b_mn) return launch_one<T, BN, STAGES, false, false, EPI>(ta, tb, a, grid, s);
-    if (k.a_mn && k.b_mn) return launch_one<T, BN, STAGES, true, true, EPI>(ta, tb, a, grid, s);
-    return launch_one<T, BN, STAGES, true, false, EPI>(ta, tb, a, grid, s);
+    if (!k.a_mn && !k.b_mn) return AEGIS_UMMA_LAUNCH(false, false);
+    if (k.a_mn && k.b_mn) return AEGIS_UMMA_LAUNCH(true, true);
+    return AEGIS_UMMA_LAUNCH(true, false);
   }
+#undef AEGIS_UMMA_LAUNCH
   return cudaErrorNotSupported;
 }
 
-template <class T, int BN, int STAGES>
+template <class T, int BN, int STAGES, bool PAIR>
 cudaError_t launch_epi(const LaunchKey& k, const CUtensorMap& ta, const CUtensorMap& tb, const Args& a, int grid,
                        cudaStream_t s) {
   switch (k.epi) {
-    case kEpiStore: return launch_layouts<T, BN, STAGES, kEpiStore>(k, ta, tb, a, grid, s);
-    case kEpiPartial: return launch_layouts<T, BN, STAGES, kEpiPartial>(k, ta, tb, a, grid, s);
+    case kEpiStore: return launch_layouts<T, BN, STAGES, kEpiStore, PAIR>(k, ta, tb, a, grid, s);
+    case kEpiPartial: return launch_layouts<T, BN, STAGES, kEpiPartial, PAIR>(k, ta, tb, a, grid, s);
     case kEpiPeers:
-      if constexpr (BN == 256) return launch_layouts<T, BN, STAGES, kEpiPeers>(k, ta, tb, a, grid, s);
+      if constexpr (BN == 256) return launch_layouts<T, BN, STAGES, kEpiPeers, PAIR>(k, ta, tb, a, grid, s);
       return cudaErrorNotSupported;
     default: return cudaErrorInvalidValue;
   }
 }
 
-// The instantiations the registry lists (gemm::UMMA_CONFIGS): (256, 4), (128, 6).
+// The instantiations the registry lists (gemm::UMMA_CONFIGS): one CTA (256, 4)
+// and (128, 6); CTA pairs (256, 6).
 template <class T>
 cudaError_t launch_family(const LaunchKey& k, const CUtensorMap& ta, const CUtensorMap& tb, const Args& a,
                           int grid, cudaStream_t s) {
-  if (k.BN == 256 && k.STAGES == 4) return launch_epi<T, 256, 4>(k, ta, tb, a, grid, s);
-  if (k.BN == 128 && k.STAGES == 6) return launch_epi<T, 128, 6>(k, ta, tb, a, grid, s);
+  if (k.pair) {
+    if (k.BN == 256 && k.STAGES == 6) return launch_epi<T, 256, 6, true>(k, ta, tb, a, grid, s);
+    return cudaErrorNotSupported;
+  }
+  if (k.BN == 256 && k.STAGES == 4) return launch_epi<T, 256, 4, false>(k, ta, tb, a, grid, s);
+  if (k.BN == 128 && k.STAGES == 6) return launch_epi<T, 128, 6, false>(k, ta, tb, a, grid, s);
   return cudaErrorNotSupported;
 }
 
 template <class T>
-cudaError_t attrs_family(int BN, int STAGES, cudaFuncAttributes* attrs) {
+cudaError_t attrs_family(int BN, int STAGES, bool pair, cudaFuncAttributes* attrs) {
+  if (pair && BN == 256 && STAGES == 6) {
+    const cudaError_t e = cudaFuncGetAttributes(attrs, &umma2_gemm_kernel<T, 256, 6, false, true, kEpiStore>);
+    if (e == cudaSuccess) attrs->sharedSizeBytes += LayoutPair<256, 6>::ALLOC;
+    return e;
+  }
   if (BN == 256 && STAGES == 4) return attrs_one<T, 256, 4, false, true, kEpiStore>(attrs);
   if (BN == 128 && STAGES == 6) return attrs_one<T, 128, 6, false, true, kEpiStore>(attrs);
   return cudaErrorNotSupported;
@@ -79,7 +118,7 @@ extern template cudaError_t launch_family<__half>(const LaunchKey&, const CUtens
                                                   const Args&, int, cudaStream_t);
 extern template cudaError_t launch_family<__nv_bfloat16>(const LaunchKey&, const CUtensorMap&, const CUtensorMap&,
                                                          const Args&, int, cudaStream_t);
-extern template cudaError_t attrs_family<__half>(int, int, cudaFuncAttributes*);
-extern template cudaError_t attrs_family<__nv_bfloat16>(int, int, cudaFuncAttributes*);
+extern template cudaError_t attrs_family<__half>(int, int, bool, cudaFuncAttributes*);
+extern template cudaError_t attrs_family<__nv_bfloat16>(int, int, bool, cudaFuncAttributes*);
 
 }  // namespace aegis::umma

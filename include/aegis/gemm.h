@@ -108,20 +108,25 @@ const KernelEntry* find(std::string_view name);
 
 // ---------------------------------------------------------------------------
 // umma family: tcgen05.mma kind::f16 (f16 or bf16 operands, FP32 accumulator
-// in TMEM), cta_group::1, BM = 128 rows (TMEM lanes) x BN columns, BK = 64
-// (one 128-byte swizzle row of 16-bit elements per k-block), STAGES-deep TMA
-// ring. Persistent: one CTA per SM walks the tile list. TMEM holds two
-// accumulators, so the epilogue of a tile overlaps the main loop of the next.
+// in TMEM), BK = 64 (one 128-byte swizzle row of 16-bit elements per
+// k-block), STAGES-deep TMA ring, persistent tile walk, two TMEM accumulators
+// (the epilogue of a tile overlaps the main loop of the next).
+// CTAS = 1: one CTA per SM, BM = 128 rows (cta_group::1).
+// CTAS = 2: a cluster of two CTAs on two SMs shares one BM = 256 tile
+//           (cta_group::2: each CTA loads half of A and half of B; the leader
+//           issues M = 256 MMAs into both CTAs' TMEM). No TMA multicast.
 // SPLITK: 0 = never split K; 1 = split K by the SM count when the tile count
 // alone cannot fill the GPU (partials reduced in a fixed order, bit-identical
-// across runs). Name: umma_<BM>x<BN>x<BK>_s<STAGES>[_ksm].
+// across runs). Name: umma_<BM>x<BN>x<BK>_s<STAGES>[_c2][_ksm].
 // ---------------------------------------------------------------------------
-struct UmmaConfig { int BM, BN, BK, STAGES, SPLITK; };
+struct UmmaConfig { int BM, BN, BK, STAGES, SPLITK, CTAS; };
 inline constexpr UmmaConfig UMMA_CONFIGS[] = {
-    {128, 256, 64, 4, 0},
-    {128, 128, 64, 6, 0},
-    {128, 256, 64, 4, 1},
-    {128, 128, 64, 6, 1},
+    {128, 256, 64, 4, 0, 1},
+    {128, 128, 64, 6, 0, 1},
+    {128, 256, 64, 4, 1, 1},
+    {128, 128, 64, 6, 1, 1},
+    {256, 256, 64, 6, 0, 2},
+    {256, 256, 64, 6, 1, 2},
 };
 std::span<const KernelEntry> umma_entries();
 
