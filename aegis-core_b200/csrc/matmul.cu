@@ -70,8 +70,11 @@ const gemm::KernelEntry* rule_for(const gemm::GemmParams& p, const gemm::DeviceC
     return by_name("gemv_64x256_ksm");
   }
   if (gemm::tma_compatible(p) && caps.arch == 100) {
+    // CTA pairs (256 x 256 tiles) measured fastest from 4096^2 up; a single
+    // CTA's 128-row tile wastes less when M or N is small.
     if (p.N <= 128) return by_name("umma_128x128x64_s6_ksm");
-    return by_name("umma_128x256x64_s4_ksm");
+    if (p.M <= 128) return by_name("umma_128x256x64_s4_ksm");
+    return by_name("umma_256x256x64_s7_c2_ksm");
   }
   return by_name("simt_64x64x16");
 }

@@ -54,6 +54,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread may sleep up to `hint_ns`
+// and resumes when the phase completes, so long waits (an epilogue waiting
+// for a whole main loop) cost neither issue slots nor power.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Suspend hint of the bounded waits below (nanoseconds).
+inline constexpr uint32_t kWaitSleepHintNs = 20000;
+
 // Bounded wait for the phase of parity `parity` to complete. Returns false,
 // without waiting further, if *abort is already set or becomes set, or when
 // `limit_ns` of %globaltimer pass; in the latter case it sets *abort (so the
@@ -64,8 +82,8 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 63u) == 0) {
+    if (mbar_try_wait_sleep(bar, parity, kWaitSleepHintNs)) return true;
+    if ((i & 7u) == 0) {
       if (*abort) return false;
       if ((long long)(globaltimer() - t0) > limit_ns) {
         *abort = 1;

@@ -52,9 +52,9 @@ __device__ __forceinline__ Unit decode_unit_pair(const Args& a, long long u) {
   const long long per_batch = (long long)a.tiles_m * a.tiles_n;
   r.b = int(tile / per_batch);
   const int t = int(tile % per_batch);
-  const int span = kGroupM * a.tiles_n;
-  const int first_m = (t / span) * kGroupM;
-  const int gsize = min(a.tiles_m - first_m, kGroupM);
+  const int span = a.group_m * a.tiles_n;
+  const int first_m = (t / span) * a.group_m;
+  const int gsize = min(a.tiles_m - first_m, a.group_m);
   const int rr = t % span;
   r.m0 = (first_m + rr % gsize) * BM_PAIR;
   r.n0 = (rr / gsize) * BN;
@@ -114,20 +114,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------ TMA producer (both CTAs)
+    // One lane runs the whole loop: a warp-wide shuffle or __syncwarp per
+    // k-block measured ~100 cycles of the ~512 a k-block's MMAs take.
     int stage = 0;
     uint32_t phase = 0, filled = 0, fill_parity = 0;
     bool ok = true;
-    for (long long unit = cluster; unit < a.units && ok; unit += nclusters) {
-      const Unit u = decode_unit_pair<BN>(a, unit);
-      const int za = a.a_batched ? u.b : 0, zb = a.b_batched ? u.b : 0;
-      const int my_m = u.m0 + 128 * int(rank), my_n = u.n0 + BNH * int(rank);
-      for (int i = 0; i < u.nkb; ++i) {
-        if (lane == 0)
+    if (lane == 0) {
+      for (long long unit = cluster; unit < a.units && ok; unit += nclusters) {
+        const Unit u = decode_unit_pair<BN>(a, unit);
+        const int za = a.a_batched ? u.b : 0, zb = a.b_batched ? u.b : 0;
+        const int my_m = u.m0 + 128 * int(rank), my_n = u.n0 + BNH * int(rank);
+        for (int i = 0; i < u.nkb; ++i) {
           ok = ptx::mbar_wait_bounded(empty_bar(stage), phase ^ 1u, abort_flag, a.status, kStatusTimeoutProducer,
                                       a.wait_limit_ns);
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok) break;
-        if (lane == 0) {
+          if (!ok) break;
           const int k0 = (u.kb0 + i) * BK;
           if (rank == 0) ptx::mbar_arrive_expect_tx(full_bar(stage), 2 * L::STAGE_TX);
           const uint32_t fb = ptx::map_to_rank(full_bar(stage), 0);  // the leader's barrier
@@ -147,18 +147,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           filled |= 1u << stage;
           fill_parity = (fill_parity & ~(1u << stage)) | (phase << stage);
-        }
-        __syncwarp();
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1u;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
         }
       }
-    }
-    // Teardown: every copy this CTA issued has landed. The leader sees its
-    // barrier complete; the peer sees the stage released by the leader's MMA
-    // (which waited for the bytes). Immediate on the normal path.
-    if (lane == 0)
+      // Teardown: every copy this CTA issued has landed. The leader sees its
+      // barrier complete; the peer sees the stage released by the leader's MMA
+      // (which waited for the bytes). Immediate on the normal path.
       for (int s = 0; s < STAGES; ++s)
         if (filled & (1u << s)) {
           const uint32_t par = (fill_parity >> s) & 1u;
@@ -166,6 +163,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                       : ptx::mbar_wait_teardown(empty_bar(s), par, a.wait_limit_ns);
           if (!done && a.status) atomicOr(a.status, kStatusTimeoutDrain);
         }
+    }
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------ MMA issuer (leader only)
@@ -176,23 +174,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0, acc = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
-      for (long long unit = cluster; unit < a.units && ok; unit += nclusters) {
-        const Unit u = decode_unit_pair<BN>(a, unit);
-        if (lane == 0)
+      if (lane == 0) {  // one lane issues everything (see the producer)
+        for (long long unit = cluster; unit < a.units && ok; unit += nclusters) {
+          const Unit u = decode_unit_pair<BN>(a, unit);
           ok = ptx::mbar_wait_bounded(tempty_bar(acc), acc_phase ^ 1u, abort_flag, a.status, kStatusTimeoutMma,
                                       a.wait_limit_ns);
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok) break;
-        ptx::tc_fence_after();
-        const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
-        for (int i = 0; i < u.nkb; ++i) {
-          if (lane == 0)
-            ok = ptx::mbar_wait_bounded(full_bar(stage), phase, abort_flag, a.status, kStatusTimeoutMma,
-                                        a.wait_limit_ns);
-          ok = __shfl_sync(0xffffffffu, ok, 0);
           if (!ok) break;
           ptx::tc_fence_after();
-          if (lane == 0) {
+          const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
+          for (int i = 0; i < u.nkb; ++i) {
+            ok = ptx::mbar_wait_bounded(full_bar(stage), phase, abort_flag, a.status, kStatusTimeoutMma,
+                                        a.wait_limit_ns);
+            if (!ok) break;
+            ptx::tc_fence_after();
             const uint32_t sa = sbase + L::A_OFF + stage * L::A_BYTES;
             const uint32_t sb = sbase + L::B_OFF + stage * L::B_BYTES;
 #pragma unroll
@@ -202,19 +196,18 @@ __global__ void __launch_bounds__(kThreads, 1)
               ptx::umma_f16_pair(d_tmem, ad, bd, idesc, (i > 0 || ks > 0) ? 1u : 0u);
             }
             ptx::umma_commit_pair(empty_bar(stage), 0x3);  // both CTAs' stage is free
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1u;
+            }
           }
-          __syncwarp();
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
+          if (!ok) break;
+          ptx::umma_commit_pair(tfull_bar(acc), 0x3);  // both halves of the accumulator ready
+          acc ^= 1;
+          if (acc == 0) acc_phase ^= 1u;
         }
-        if (!ok) break;
-        if (lane == 0) ptx::umma_commit_pair(tfull_bar(acc), 0x3);  // both halves of the accumulator ready
-        __syncwarp();
-        acc ^= 1;
-        if (acc == 0) acc_phase ^= 1u;
       }
+      __syncwarp();
     }
   } else {
     // ------------------------------------------------ epilogue (warps 2..5, both CTAs)

@@ -11,6 +11,7 @@
 // alone, so here every SM shares the (L2-resident) reduction.
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -139,9 +140,22 @@ struct Plan {
   int BM = 128, BN = 256, STAGES = 4, CTAS = 1;
   int splits = 1, kb_per_split = 0, kb_total = 0;
   int tiles_m = 0, tiles_n = 0;
+  int group_m = umma::kGroupM;
   long long tiles = 0, units = 0;
   int grid = 0;
 };
+
+// Raster group (tile rows walked together before moving along N). The
+// AEGIS_UMMA_GROUP_M environment variable overrides the default, read once,
+// for tuning sweeps; values outside [1, 64] are ignored.
+int group_m_default() {
+  static const int g = [] {
+    const char* s = std::getenv("AEGIS_UMMA_GROUP_M");
+    const int v = s ? std::atoi(s) : 0;
+    return v >= 1 && v <= 64 ? v : umma::kGroupM;
+  }();
+  return g;
+}
 
 // CTA pairs that can be resident at once on the current device (both CTAs of
 // a cluster must sit in one GPC), queried once per device; sms/2 if the query
@@ -159,7 +173,7 @@ int pair_slots(int sms) {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(unsigned(2 * sms));
     cfg.blockDim = dim3(umma::kThreads);
-    cfg.dynamicSmemBytes = umma::LayoutPair<256, 6>::ALLOC;
+    cfg.dynamicSmemBytes = umma::LayoutPair<256, gemm::kUmmaPairStages>::ALLOC;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
@@ -167,9 +181,9 @@ int pair_slots(int sms) {
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    auto* kern = &umma::umma2_gemm_kernel<__nv_bfloat16, 256, 6, false, true, umma::kEpiStore>;
+    auto* kern = &umma::umma2_gemm_kernel<__nv_bfloat16, 256, gemm::kUmmaPairStages, false, true, umma::kEpiStore>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             int(umma::LayoutPair<256, 6>::ALLOC)) != cudaSuccess ||
+                             int(umma::LayoutPair<256, gemm::kUmmaPairStages>::ALLOC)) != cudaSuccess ||
         cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
       cudaGetLastError();
       n = sms;
@@ -188,6 +202,7 @@ Plan make_plan(int cfg, const GemmParams& p) {
   pl.CTAS = c.CTAS;
   pl.tiles_m = ceil_div(p.M, c.BM);
   pl.tiles_n = ceil_div(p.N, c.BN);
+  pl.group_m = group_m_default();
   pl.kb_total = ceil_div(p.K, umma::BK);
   pl.tiles = (long long)p.batch * pl.tiles_m * pl.tiles_n;
   const hw::DeviceLimits* d = hw::current();
@@ -222,6 +237,7 @@ umma::Args make_args(const GemmParams& p, const Plan& pl) {
   a.b_batched = p.batch > 1 && p.stride_b != 0;
   a.tiles_m = pl.tiles_m;
   a.tiles_n = pl.tiles_n;
+  a.group_m = pl.group_m;
   a.splits = pl.splits;
   a.kb_per_split = pl.kb_per_split;
   a.kb_total = pl.kb_total;
@@ -240,6 +256,14 @@ cudaError_t launch(const GemmParams& p, const umma::LaunchKey& k, const Maps& m,
   return p.dtype == DType::BF16 ? umma::launch_family<__nv_bfloat16>(k, m.a, m.b, a, grid, s)
                                 : umma::launch_family<__half>(k, m.a, m.b, a, grid, s);
 }
+
+// The N-sharded GEMM runs UMMA_CONFIGS[4]: CTA pairs, 256 x 256 tiles, no
+// split-K (measured equal to or faster than one-CTA 128 x 256 tiles at
+// 4096^3 .. 16384^3).
+constexpr int kNshardConfig = 4;
+static_assert(gemm::UMMA_CONFIGS[kNshardConfig].CTAS == 2 && gemm::UMMA_CONFIGS[kNshardConfig].BN == 256 &&
+                  !gemm::UMMA_CONFIGS[kNshardConfig].SPLITK,
+              "the N-sharded path needs the non-split CTA-pair config");
 
 bool device_is_sm100() {
   const hw::DeviceLimits* d = hw::physical();
@@ -289,7 +313,7 @@ cudaError_t umma_attrs(int cfg, cudaFuncAttributes* attrs) {
 
 size_t umma_smem_bytes(int cfg) {
   const gemm::UmmaConfig& c = gemm::UMMA_CONFIGS[cfg];
-  if (c.CTAS == 2) return size_t(umma::LayoutPair<256, 6>::ALLOC);
+  if (c.CTAS == 2) return size_t(umma::LayoutPair<256, gemm::kUmmaPairStages>::ALLOC);
   return c.BN == 256 ? size_t(umma::Layout<256, 4>::ALLOC) : size_t(umma::Layout<128, 6>::ALLOC);
 }
 
@@ -299,9 +323,9 @@ cudaError_t umma_nsharded(const GemmParams& local, void* const* c_ranks, int nra
   if (!gemm::tma_compatible(local) || !device_is_sm100()) return cudaErrorNotSupported;
   if (local.layout_a != Layout::RowMajor || local.layout_b != Layout::RowMajor || local.batch != 1)
     return cudaErrorInvalidValue;
-  const Plan pl = make_plan(0, local);  // 128 x 256 tiles, no split
+  const Plan pl = make_plan(kNshardConfig, local);  // CTA pairs, 256 x 256 tiles, no split
   Maps maps;
-  if (!make_maps(local, pl.BN, &maps)) return cudaErrorNotSupported;
+  if (!make_maps(local, pl.CTAS == 2 ? pl.BN / 2 : pl.BN, &maps)) return cudaErrorNotSupported;
   umma::Args a = make_args(local, pl);
   if (const cudaError_t e = status::word(&a.status); e != cudaSuccess) return e;
   a.npeers = nranks;
@@ -310,7 +334,7 @@ cudaError_t umma_nsharded(const GemmParams& local, void* const* c_ranks, int nra
     if (!c_ranks[i]) return cudaErrorInvalidValue;
     a.peers[i] = c_ranks[i];
   }
-  const umma::LaunchKey k{pl.BN, pl.STAGES, false, true, umma::kEpiPeers};
+  const umma::LaunchKey k{pl.BN, pl.STAGES, false, true, umma::kEpiPeers, pl.CTAS == 2};
   return launch(local, k, maps, a, pl.grid, stream);
 }
 

@@ -7,7 +7,7 @@
 // Replaces the reference's best large-GEMM kernel, gemm_mma_tma_kernel
 // (src/gemm/mma_tma.cu:171-228: TMA box loads into an mbarrier ring feeding
 // mma.sync from every warp), with the Blackwell structure:
-//   warp 0      TMA producer: one elected lane fills a STAGES-deep ring of
+//   warp 0      TMA producer: lane 0 alone fills a STAGES-deep ring of
 //               (A tile, B tile) k-blocks, mbarrier complete_tx;
 //   warp 1      allocates 2*BN TMEM columns; one lane issues tcgen05.mma
 //               (M=128, N=BN, K=16) for every k-block and commits each stage
@@ -45,7 +45,7 @@ namespace aegis::umma {
 inline constexpr int BM = 128;
 inline constexpr int BK = 64;  // 64 16-bit elements = one 128-byte swizzle row
 inline constexpr int kThreads = 192;
-inline constexpr int kGroupM = 8;
+inline constexpr int kGroupM = 8;  // default raster group (tile rows)
 inline constexpr int kMaxPeers = 8;
 
 enum Epi : int { kEpiStore = 0, kEpiPartial = 1, kEpiPeers = 2 };
@@ -55,6 +55,7 @@ struct Args {
   int batch;
   int a_batched, b_batched;  // use the batch coordinate for A / B loads
   int tiles_m, tiles_n;
+  int group_m;      // tile rows per raster group (>= 1)
   int splits, kb_per_split, kb_total;
   long long units;  // batch * tiles_m * tiles_n * splits
   void* C;
@@ -96,9 +97,9 @@ __device__ __forceinline__ Unit decode_unit(const Args& a, long long u) {
   const long long per_batch = (long long)a.tiles_m * a.tiles_n;
   r.b = int(tile / per_batch);
   const int t = int(tile % per_batch);
-  const int span = kGroupM * a.tiles_n;
-  const int first_m = (t / span) * kGroupM;
-  const int gsize = min(a.tiles_m - first_m, kGroupM);
+  const int span = a.group_m * a.tiles_n;
+  const int first_m = (t / span) * a.group_m;
+  const int gsize = min(a.tiles_m - first_m, a.group_m);
   const int rr = t % span;
   r.m0 = (first_m + rr % gsize) * BM;
   r.n0 = (rr / gsize) * BN;
@@ -217,20 +218,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------ TMA producer
-    int stage = 0;
-    uint32_t phase = 0;
-    uint32_t filled = 0, fill_parity = 0;  // per stage: ever filled / parity of the last fill
-    for (long long unit = blockIdx.x; unit < a.units; unit += gridDim.x) {
-      const Unit u = decode_unit<BN>(a, unit);
-      const int za = a.a_batched ? u.b : 0, zb = a.b_batched ? u.b : 0;
+    // One lane runs the whole loop: a warp-wide shuffle or __syncwarp per
+    // k-block measured ~100 cycles of the ~512 a k-block's MMAs take.
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t filled = 0, fill_parity = 0;  // per stage: ever filled / parity of the last fill
       bool ok = true;
-      for (int i = 0; i < u.nkb && ok; ++i) {
-        if (lane == 0)
+      for (long long unit = blockIdx.x; unit < a.units && ok; unit += gridDim.x) {
+        const Unit u = decode_unit<BN>(a, unit);
+        const int za = a.a_batched ? u.b : 0, zb = a.b_batched ? u.b : 0;
+        for (int i = 0; i < u.nkb; ++i) {
           ok = ptx::mbar_wait_bounded(empty_bar(stage), phase ^ 1u, abort_flag, a.status, kStatusTimeoutProducer,
                                       a.wait_limit_ns);
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok) break;
-        if (lane == 0) {
+          if (!ok) break;
           const int k0 = (u.kb0 + i) * BK;
           const uint32_t fb = full_bar(stage);
           ptx::mbar_arrive_expect_tx(fb, L::STAGE_TX);
@@ -250,18 +251,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           filled |= 1u << stage;
           fill_parity = (fill_parity & ~(1u << stage)) | (phase << stage);
-        }
-        __syncwarp();
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1u;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
         }
       }
-      if (!ok) break;
-    }
-    // Teardown: every copy this CTA issued has landed before shared memory
-    // is released (immediate on the normal path: the MMA warp consumed them).
-    if (lane == 0) {
+      // Teardown: every copy this CTA issued has landed before shared memory
+      // is released (immediate on the normal path: the MMA warp consumed them).
       for (int s = 0; s < STAGES; ++s)
         if (filled & (1u << s))
           if (!ptx::mbar_wait_teardown(full_bar(s), (fill_parity >> s) & 1u, a.wait_limit_ns) && a.status)
@@ -277,28 +274,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Advance per K=16 step: 32 B inside the swizzled row (K-major), or 16
     // k-rows of 128 B (MN-major).
     constexpr uint32_t a_kstep = A_MN ? 2048u : 32u, b_kstep = B_MN ? 2048u : 32u;
-    int stage = 0;
-    uint32_t phase = 0;
-    int acc = 0;
-    uint32_t acc_phase = 0;
-    for (long long unit = blockIdx.x; unit < a.units; unit += gridDim.x) {
-      const Unit u = decode_unit<BN>(a, unit);
+    if (lane == 0) {  // one lane issues everything (see the producer)
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
       bool ok = true;
-      if (lane == 0)
+      for (long long unit = blockIdx.x; unit < a.units && ok; unit += gridDim.x) {
+        const Unit u = decode_unit<BN>(a, unit);
         ok = ptx::mbar_wait_bounded(tempty_bar(acc), acc_phase ^ 1u, abort_flag, a.status, kStatusTimeoutMma,
                                     a.wait_limit_ns);
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
-      ptx::tc_fence_after();
-      const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
-      for (int i = 0; i < u.nkb && ok; ++i) {
-        if (lane == 0)
-          ok = ptx::mbar_wait_bounded(full_bar(stage), phase, abort_flag, a.status, kStatusTimeoutMma,
-                                      a.wait_limit_ns);
-        ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) break;
         ptx::tc_fence_after();
-        if (lane == 0) {
+        const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
+        for (int i = 0; i < u.nkb; ++i) {
+          ok = ptx::mbar_wait_bounded(full_bar(stage), phase, abort_flag, a.status, kStatusTimeoutMma,
+                                      a.wait_limit_ns);
+          if (!ok) break;
+          ptx::tc_fence_after();
           const uint32_t sa = sbase + L::A_OFF + stage * L::A_BYTES;
           const uint32_t sb = sbase + L::B_OFF + stage * L::B_BYTES;
 #pragma unroll
@@ -308,19 +301,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::umma_f16(d_tmem, ad, bd, idesc, (i > 0 || ks > 0) ? 1u : 0u);
           }
           ptx::umma_commit(empty_bar(stage));  // frees the stage once these MMAs have read it
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
         }
-        __syncwarp();
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1u;
-        }
+        if (!ok) break;
+        ptx::umma_commit(tfull_bar(acc));  // accumulator complete
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
       }
-      if (!ok) break;
-      if (lane == 0) ptx::umma_commit(tfull_bar(acc));  // accumulator complete
-      __syncwarp();
-      acc ^= 1;
-      if (acc == 0) acc_phase ^= 1u;
     }
+    __syncwarp();
   } else {
     // ------------------------------------------------ epilogue (warps 2..5)
     const int quarter = warp & 3;  // TMEM lanes this warp may access

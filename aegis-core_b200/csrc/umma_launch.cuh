@@ -4,6 +4,7 @@
 // umma_f16.cu / umma_bf16.cu so the two compile in parallel.
 #include <cuda.h>
 
+#include "aegis/gemm.h"
 #include "device.h"
 #include "umma2_kernel.cuh"
 
@@ -88,12 +89,13 @@ cudaError_t launch_epi(const LaunchKey& k, const CUtensorMap& ta, const CUtensor
 }
 
 // The instantiations the registry lists (gemm::UMMA_CONFIGS): one CTA (256, 4)
-// and (128, 6); CTA pairs (256, 6).
+// and (128, 6); CTA pairs (256, gemm::kUmmaPairStages).
 template <class T>
 cudaError_t launch_family(const LaunchKey& k, const CUtensorMap& ta, const CUtensorMap& tb, const Args& a,
                           int grid, cudaStream_t s) {
   if (k.pair) {
-    if (k.BN == 256 && k.STAGES == 6) return launch_epi<T, 256, 6, true>(k, ta, tb, a, grid, s);
+    constexpr int PS = gemm::kUmmaPairStages;
+    if (k.BN == 256 && k.STAGES == PS) return launch_epi<T, 256, PS, true>(k, ta, tb, a, grid, s);
     return cudaErrorNotSupported;
   }
   if (k.BN == 256 && k.STAGES == 4) return launch_epi<T, 256, 4, false>(k, ta, tb, a, grid, s);
@@ -103,9 +105,10 @@ cudaError_t launch_family(const LaunchKey& k, const CUtensorMap& ta, const CUten
 
 template <class T>
 cudaError_t attrs_family(int BN, int STAGES, bool pair, cudaFuncAttributes* attrs) {
-  if (pair && BN == 256 && STAGES == 6) {
-    const cudaError_t e = cudaFuncGetAttributes(attrs, &umma2_gemm_kernel<T, 256, 6, false, true, kEpiStore>);
-    if (e == cudaSuccess) attrs->sharedSizeBytes += LayoutPair<256, 6>::ALLOC;
+  constexpr int PS = gemm::kUmmaPairStages;
+  if (pair && BN == 256 && STAGES == PS) {
+    const cudaError_t e = cudaFuncGetAttributes(attrs, &umma2_gemm_kernel<T, 256, PS, false, true, kEpiStore>);
+    if (e == cudaSuccess) attrs->sharedSizeBytes += LayoutPair<256, PS>::ALLOC;
     return e;
   }
   if (BN == 256 && STAGES == 4) return attrs_one<T, 256, 4, false, true, kEpiStore>(attrs);

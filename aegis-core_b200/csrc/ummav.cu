@@ -151,18 +151,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------ TMA producer
-    int stage = 0;
-    uint32_t phase = 0, filled = 0, fill_parity = 0;
-    bool ok = true;
-    for (long long pos = r0; pos < r1 && ok;) {
-      const Seg sg = next_seg(pos);
-      for (int i = 0; i < sg.nkb; ++i) {
-        if (lane == 0)
+    // One lane runs the loop (no warp-wide shuffle or __syncwarp per k-block).
+    uint32_t filled = 0, fill_parity = 0;
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (long long pos = r0; pos < r1 && ok;) {
+        const Seg sg = next_seg(pos);
+        for (int i = 0; i < sg.nkb; ++i) {
           ok = ptx::mbar_wait_bounded(empty_bar(stage), phase ^ 1u, abort_flag, a.status, kStatusTimeoutProducer,
                                       a.wait_limit_ns);
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok) break;
-        if (lane == 0) {
+          if (!ok) break;
           const int k0 = (sg.kb0 + i) * BK;
           const uint32_t fb = full_bar(stage);
           ptx::mbar_arrive_expect_tx(fb, L::STAGE_TX);
@@ -172,15 +172,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           ptx::tma_load_3d(sbase + L::A_OFF + stage * L::A_BYTES, &tmA, fb, k0, 0, 0);
           filled |= 1u << stage;
           fill_parity = (fill_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
         }
-        __syncwarp();
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1u;
-        }
+        pos += sg.nkb;
       }
-      pos += sg.nkb;
     }
+    __syncwarp();
     ptx::griddep_launch_dependents();  // every load is issued: dependents may start their prologue
     if (lane == 0)
       for (int s = 0; s < STAGES; ++s)
@@ -189,28 +189,24 @@ __global__ void __launch_bounds__(kThreads, 1)
             atomicOr(a.status, kStatusTimeoutDrain);
     __syncwarp();
   } else if (warp == 1) {
-    // ------------------------------------------------ MMA issuer
+    // ------------------------------------------------ MMA issuer (one lane)
     constexpr uint32_t idesc = ptx::umma_idesc_f16(Elem<T>::kBf16, /*a MN-major*/ true, /*b K-major*/ false, BMN, MPAD);
-    int stage = 0, acc = 0;
-    uint32_t phase = 0, acc_phase = 0;
-    bool ok = true;
-    for (long long pos = r0; pos < r1 && ok;) {
-      const Seg sg = next_seg(pos);
-      if (lane == 0)
+    if (lane == 0) {
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (long long pos = r0; pos < r1 && ok;) {
+        const Seg sg = next_seg(pos);
         ok = ptx::mbar_wait_bounded(tempty_bar(acc), acc_phase ^ 1u, abort_flag, a.status, kStatusTimeoutMma,
                                     a.wait_limit_ns);
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
-      ptx::tc_fence_after();
-      const uint32_t d_tmem = tmem_base + uint32_t(acc * MPAD);
-      for (int i = 0; i < sg.nkb; ++i) {
-        if (lane == 0)
-          ok = ptx::mbar_wait_bounded(full_bar(stage), phase, abort_flag, a.status, kStatusTimeoutMma,
-                                      a.wait_limit_ns);
-        ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) break;
         ptx::tc_fence_after();
-        if (lane == 0) {
+        const uint32_t d_tmem = tmem_base + uint32_t(acc * MPAD);
+        for (int i = 0; i < sg.nkb; ++i) {
+          ok = ptx::mbar_wait_bounded(full_bar(stage), phase, abort_flag, a.status, kStatusTimeoutMma,
+                                      a.wait_limit_ns);
+          if (!ok) break;
+          ptx::tc_fence_after();
           const uint32_t sb = sbase + L::B_OFF + stage * L::B_BYTES;
           const uint32_t sa = sbase + L::A_OFF + stage * L::A_BYTES;
 #pragma unroll
@@ -221,20 +217,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::umma_f16(d_tmem, wd, xd, idesc, (i > 0 || ks > 0) ? 1u : 0u);
           }
           ptx::umma_commit(empty_bar(stage));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
         }
-        __syncwarp();
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1u;
-        }
+        if (!ok) break;
+        ptx::umma_commit(tfull_bar(acc));
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+        pos += sg.nkb;
       }
-      if (!ok) break;
-      if (lane == 0) ptx::umma_commit(tfull_bar(acc));
-      __syncwarp();
-      acc ^= 1;
-      if (acc == 0) acc_phase ^= 1u;
-      pos += sg.nkb;
     }
+    __syncwarp();
   } else {
     // ------------------------------------------------ epilogue (warps 2..5)
     const int quarter = warp & 3;

@@ -111,7 +111,7 @@ class ClockSampler:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-        sm, mx, reasons = [], None, set()
+        sm, mx, reasons, pw = [], None, set(), []
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for ln in self.lines:
             parts = [x.strip() for x in ln.split(",")]
@@ -122,12 +122,18 @@ class ClockSampler:
                 mx = float(parts[2])
             except ValueError:
                 continue
+            try:
+                pw.append((float(parts[1]), float(parts[3])))
+            except ValueError:
+                pass
             for nm, v in zip(names, parts[5:9]):
                 if v.lower() == "active":
                     reasons.add(nm)
         under_load = [s for s in sm if mx and s > 0.3 * mx] or sm
+        watts = [w for s, w in pw if mx and s > 0.3 * mx] or [w for _, w in pw]
         return {"sm_mhz": statistics.median(under_load) if under_load else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm),
+                "power_w": statistics.median(watts) if watts else None}
 
 
 def load_traffic(name):
@@ -353,7 +359,7 @@ def bench_nshard(args, rank, local_rank, world):
         "vs_baseline": None, "dtype": dtype, "data": "synthetic: std::mt19937(0) uniform[-1,1], A then B",
         "config": {"workload": f"config5_gemm_{dtype}_{n}^3_nshard", "M": M, "N": N, "K": K,
                    "parallelism": f"nshard{world}", "l2": "inputs larger than L2 (A = %d MiB)" % (M * K * 2 >> 20),
-                   "kernel": "umma_128x256x64_s4 (tcgen05 cta_group::1, peer-store epilogue)"},
+                   "kernel": "umma_256x256x64_s7_c2 (tcgen05 cta_group::2, peer-store epilogue)"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops_sustained"],
                      "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops_sustained"],
                      "traffic": traffic, "peak_source": f"{src} bf16_tflops_sustained",
@@ -502,7 +508,10 @@ def bench_single(args):
         dA, dB, _ = sets[i % nsets]
         torch.matmul(dA.view(tdt).view(M, K), dB.view(tdt).view(K, N), out=outs[i % nsets])
 
+    cub_clocks = ClockSampler(0)
+    cub_clocks.start()
     cublas_ms = timed(cublas, steps)
+    cub_clk = cub_clocks.stop()
     peaks, src = measured_peaks()
     flops = 2.0 * M * N * K
     choice = impl or ctx.choice(M, N, K)
@@ -529,6 +538,7 @@ def bench_single(args):
             roof["hbm_frac"] = hbm / peaks["hbm_gbs"]
         cub = {"value": flops / (cublas_ms * 1e-3) / 1e12, "unit": "TFLOP/s"}
     cub["ratio_ours_over_cublas"] = cublas_ms / ms
+    cub["clocks"] = {k: cub_clk.get(k) for k in ("sm_mhz", "power_w", "reasons")}
     line = {"metric": {"square": "GEMM TFLOP/s", "splitk": "GEMM TFLOP/s (tall-K split-K)",
                        "gemv": "GEMV HBM GB/s (weights)"}[wl],
             "value": value, "unit": unit, "n_gpus": 1, "steps": steps, "warmup": args.warmup, "ms_per_step": ms,

@@ -120,13 +120,16 @@ const KernelEntry* find(std::string_view name);
 // across runs). Name: umma_<BM>x<BN>x<BK>_s<STAGES>[_c2][_ksm].
 // ---------------------------------------------------------------------------
 struct UmmaConfig { int BM, BN, BK, STAGES, SPLITK, CTAS; };
+// Ring depth of the CTA-pair configs: 7 x 32 KB stages fill the 227 KB of
+// shared memory a CTA may use.
+inline constexpr int kUmmaPairStages = 7;
 inline constexpr UmmaConfig UMMA_CONFIGS[] = {
     {128, 256, 64, 4, 0, 1},
     {128, 128, 64, 6, 0, 1},
     {128, 256, 64, 4, 1, 1},
     {128, 128, 64, 6, 1, 1},
-    {256, 256, 64, 6, 0, 2},
-    {256, 256, 64, 6, 1, 2},
+    {256, 256, 64, kUmmaPairStages, 0, 2},
+    {256, 256, 64, kUmmaPairStages, 1, 2},
 };
 std::span<const KernelEntry> umma_entries();
 
