@@ -299,6 +299,82 @@ __device__ __forceinline__ void umma_commit_pair(uint32_t bar, uint16_t cta_mask
       : "memory");
 }
 
+// Store to another CTA's shared memory (cluster address from map_to_rank).
+__device__ __forceinline__ void st_cluster_s64(uint32_t cluster_addr, long long v) {
+  asm volatile("st.shared::cluster.s64 [%0], %1;" ::"r"(cluster_addr), "l"(v) : "memory");
+}
+__device__ __forceinline__ long long ld_shared_s64(uint32_t addr) {
+  long long v;
+  asm volatile("ld.shared.s64 %0, [%1];" : "=l"(v) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_shared_s64(uint32_t addr, long long v) {
+  asm volatile("st.shared.s64 [%0], %1;" ::"r"(addr), "l"(v) : "memory");
+}
+
+// try_wait with acquire at cluster scope: pairs with an arrive.release.cluster
+// from another CTA of the cluster (its prior shared::cluster stores are then
+// visible to this thread).
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(kWaitSleepHintNs)
+      : "memory");
+  return ok != 0;
+}
+// mbar_wait_bounded with cluster-scope acquire.
+__device__ __forceinline__ bool mbar_wait_bounded_cluster(uint32_t bar, uint32_t parity, volatile int* abort,
+                                                          unsigned* status, unsigned bit, long long limit_ns) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((i & 7u) == 0) {
+      if (*abort) return false;
+      if ((long long)(globaltimer() - t0) > limit_ns) {
+        *abort = 1;
+        if (status) {
+          atomicOr(status, bit);
+          atomicCAS(status + 1, 0u, blockIdx.x + 1u);
+        }
+        return false;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------- cluster launch control
+// Asks the hardware to cancel the launch of a cluster of this grid that has
+// not started yet; the 16-byte response lands in this CTA's shared memory at
+// `resp` (16-byte aligned) and completes 16 transaction bytes on `bar` (the
+// caller arms it with mbar_arrive_expect_tx(bar, 16) first). Once a request
+// has failed, no further request may be made.
+__device__ __forceinline__ void clc_try_cancel(uint32_t resp, uint32_t bar) {
+  asm volatile("clusterlaunchcontrol.try_cancel.async.shared::cta.mbarrier::complete_tx::bytes.b128 [%0], [%1];" ::
+                   "r"(resp),
+               "r"(bar)
+               : "memory");
+}
+// Decodes a response: the x index of the first CTA of the cancelled cluster,
+// or -1 when the request failed (no cluster was left to cancel).
+__device__ __forceinline__ int clc_first_ctaid_x(uint32_t resp) {
+  uint32_t ok, x = 0;
+  asm volatile(
+      "{\n\t.reg .b128 h;\n\t.reg .pred p;\n\t"
+      "ld.shared.b128 h, [%2];\n\t"
+      "clusterlaunchcontrol.query_cancel.is_canceled.pred.b128 p, h;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t"
+      "@p clusterlaunchcontrol.query_cancel.get_first_ctaid::x.b32.b128 %1, h;\n\t}"
+      : "=r"(ok), "+r"(x)
+      : "r"(resp)
+      : "memory");
+  return ok ? int(x) : -1;
+}
+
 // Programmatic dependent launch: wait until the grids this one depends on
 // have completed and their writes are visible (a no-op when the launch did
 // not opt in), and let dependent grids start their prologue early.

@@ -37,7 +37,8 @@ struct LayoutPair {
   static constexpr int BAR_OFF = STAGES * (A_BYTES + B_BYTES);
   static constexpr int NBARS = 2 * STAGES + 5;  // full[S], empty[S], tfull[2], tempty[2], drain
   static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;
-  static constexpr int BYTES = MISC_OFF + 16;
+  static constexpr int SCHED_OFF = (MISC_OFF + 16 + 15) / 16 * 16;  // tile schedule (tile_sched.cuh)
+  static constexpr int BYTES = SCHED_OFF + SchedSmem::BYTES;
   static constexpr int ALLOC = BYTES + 1024;
   static constexpr int TMEM_COLS = 2 * BN;
   static_assert(A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "tiles must stay 1024-byte aligned");
@@ -75,7 +76,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = int(threadIdx.x >> 5);
   const int lane = int(threadIdx.x & 31);
   const uint32_t rank = ptx::cluster_ctarank();  // 0: the pair leader
-  const long long cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+  const long long first_unit = blockIdx.x >> 1;  // one cluster per unit; later units come from the schedule
 
   const uint32_t bar0 = sbase + L::BAR_OFF;
   auto full_bar = [&](int s) { return bar0 + 8u * s; };
@@ -85,6 +86,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t drain_bar = bar0 + 8u * (2 * STAGES + 4);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::MISC_OFF);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::MISC_OFF + 4);
+  const Sched sched{sbase + L::SCHED_OFF, abort_flag, a.status, a.wait_limit_ns};
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -96,6 +98,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mbar_init(tempty_bar(acc), 256);  // every epilogue thread of both CTAs (leader's copy is used)
     }
     ptx::mbar_init(drain_bar, 1);
+    // Schedule slots are released on the leader's barrier by the leader's MMA
+    // lane and epilogue warps (1 + 4) and the peer's producer and epilogue
+    // warps (1 + 4); the peer's copy of the barrier goes unused.
+    sched.init(10);
     *abort_flag = 0;
     ptx::fence_mbar_init();
   }
@@ -120,7 +126,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t phase = 0, filled = 0, fill_parity = 0;
     bool ok = true;
     if (lane == 0) {
-      for (long long unit = cluster; unit < a.units && ok; unit += nclusters) {
+      SchedOwner owner;  // used by the leader only
+      int seq = 0;       // the peer's position in the schedule
+      for (long long unit = first_unit; ok && unit >= 0;) {
+        if (rank == 0) owner.request(sched);  // the next unit, answered while this one loads
         const Unit u = decode_unit_pair<BN>(a, unit);
         const int za = a.a_batched ? u.b : 0, zb = a.b_batched ? u.b : 0;
         const int my_m = u.m0 + 128 * int(rank), my_n = u.n0 + BNH * int(rank);
@@ -152,10 +161,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             phase ^= 1u;
           }
         }
+        if (!ok) break;
+        ok = rank == 0 ? owner.publish_next(sched, 2, true, &unit, kStatusTimeoutProducer)
+                       : sched_take(sched, seq, true, &unit, kStatusTimeoutProducer);
       }
-      // Teardown: every copy this CTA issued has landed. The leader sees its
-      // barrier complete; the peer sees the stage released by the leader's MMA
-      // (which waited for the bytes). Immediate on the normal path.
+      // Teardown: every copy this CTA issued (and a schedule request still in
+      // flight) has landed. The leader sees its barrier complete; the peer sees
+      // the stage released by the leader's MMA (which waited for the bytes).
+      // Immediate on the normal path.
+      owner.drain(sched);
       for (int s = 0; s < STAGES; ++s)
         if (filled & (1u << s)) {
           const uint32_t par = (fill_parity >> s) & 1u;
@@ -175,7 +189,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
       if (lane == 0) {  // one lane issues everything (see the producer)
-        for (long long unit = cluster; unit < a.units && ok; unit += nclusters) {
+        int seq = 0;
+        for (long long unit = first_unit; ok && unit >= 0;) {
           const Unit u = decode_unit_pair<BN>(a, unit);
           ok = ptx::mbar_wait_bounded(tempty_bar(acc), acc_phase ^ 1u, abort_flag, a.status, kStatusTimeoutMma,
                                       a.wait_limit_ns);
@@ -205,6 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ptx::umma_commit_pair(tfull_bar(acc), 0x3);  // both halves of the accumulator ready
           acc ^= 1;
           if (acc == 0) acc_phase ^= 1u;
+          ok = sched_take(sched, seq, false, &unit, kStatusTimeoutMma);
         }
       }
       __syncwarp();
@@ -216,7 +232,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
-    for (long long unit = cluster; unit < a.units && ok; unit += nclusters) {
+    int seq = 0;
+    for (long long unit = first_unit; ok && unit >= 0;) {
       const Unit u = decode_unit_pair<BN>(a, unit);
       if (lane == 0)
         ok = ptx::mbar_wait_bounded(tfull_bar(acc), acc_phase, abort_flag, a.status, kStatusTimeoutEpilogue,
@@ -238,6 +255,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mbar_arrive_cluster(ptx::map_to_rank(tempty_bar(acc), 0));  // this half of the accumulator is free
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
+      long long next = -1;
+      if (lane == 0) ok = sched_take(sched, seq, rank != 0, &next, kStatusTimeoutEpilogue);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      unit = __shfl_sync(0xffffffffu, next, 0);
     }
     if constexpr (EPI == kEpiPeers) __threadfence_system();
   }

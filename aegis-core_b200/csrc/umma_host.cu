@@ -136,6 +136,10 @@ cudaError_t launch_reduce(const float* part, int S, const GemmParams& p, cudaStr
 }
 
 // ---------------------------------------------------------------- planning
+// Units one launch can take (one cluster each, grid.x < 2^31). Far above
+// any problem that fits in device memory; larger plans are refused.
+constexpr long long kMaxUnits = 1ll << 29;
+
 struct Plan {
   int BM = 128, BN = 256, STAGES = 4, CTAS = 1;
   int splits = 1, kb_per_split = 0, kb_total = 0;
@@ -222,8 +226,9 @@ Plan make_plan(int cfg, const GemmParams& p) {
   pl.kb_per_split = ceil_div(pl.kb_total, S);
   pl.splits = ceil_div(pl.kb_total, pl.kb_per_split);
   pl.units = pl.tiles * pl.splits;
-  const long long g = sms > 0 ? std::min<long long>(pl.units, sms) : pl.units;
-  pl.grid = int(std::max<long long>(1, g)) * c.CTAS;  // CTAs (pairs: two per tile slot)
+  // One CTA (pair: one cluster of two) per unit: the CTAs that fit run and
+  // take the rest in launch order (tile_sched.cuh).
+  pl.grid = int(std::max<long long>(1, std::min<long long>(pl.units, kMaxUnits))) * c.CTAS;
   return pl;
 }
 
@@ -278,6 +283,7 @@ cudaError_t umma_run(int cfg, const GemmParams& p, cudaStream_t stream) {
   if (p.alpha == 0.f) return scale_c(p, stream);
   if (!gemm::tma_compatible(p) || !device_is_sm100()) return simt_run(p, stream);
   const Plan pl = make_plan(cfg, p);
+  if (pl.units > kMaxUnits) return cudaErrorInvalidValue;
   Maps maps;
   if (!make_maps(p, pl.CTAS == 2 ? pl.BN / 2 : pl.BN, &maps)) return simt_run(p, stream);  // TMA refused the geometry
   umma::Args a = make_args(p, pl);
@@ -324,6 +330,7 @@ cudaError_t umma_nsharded(const GemmParams& local, void* const* c_ranks, int nra
   if (local.layout_a != Layout::RowMajor || local.layout_b != Layout::RowMajor || local.batch != 1)
     return cudaErrorInvalidValue;
   const Plan pl = make_plan(kNshardConfig, local);  // CTA pairs, 256 x 256 tiles, no split
+  if (pl.units > kMaxUnits) return cudaErrorInvalidValue;
   Maps maps;
   if (!make_maps(local, pl.CTAS == 2 ? pl.BN / 2 : pl.BN, &maps)) return cudaErrorNotSupported;
   umma::Args a = make_args(local, pl);

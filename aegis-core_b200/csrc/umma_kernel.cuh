@@ -17,10 +17,12 @@
 //               lanes 32*(w%4)..+31, i.e. tile rows), FP32 -> alpha/beta ->
 //               16-bit, stores to C; or FP32 partials (split-K); or the same
 //               16-bit tile stored to every rank's C (N-sharded all-gather).
-// Persistent: gridDim.x <= #SMs CTAs, each walks units blockIdx.x,
-// +gridDim.x, ... in a grouped raster (8 M-tiles per group) so concurrently
-// running tiles share A and B in L2. Two TMEM accumulators let the epilogue
-// of one tile overlap the main loop of the next.
+// Persistent with an in-order dynamic schedule (tile_sched.cuh): one CTA per
+// unit is launched; the CTAs that fit run their own unit, then take the
+// not-yet-started ones in launch order (cluster launch control), walking a
+// grouped raster (Args::group_m M-tiles per group) so concurrently running
+// tiles share A and B in L2. Two TMEM accumulators let the epilogue of one
+// tile overlap the main loop of the next.
 //
 // Operand layouts in shared memory (128-byte swizzle, TMA writes them):
 //   A row-major  (K-major): one box [128 rows][64 k]          16 KB
@@ -39,6 +41,7 @@
 
 #include "common.cuh"
 #include "ptx.cuh"
+#include "tile_sched.cuh"
 
 namespace aegis::umma {
 
@@ -78,7 +81,8 @@ struct Layout {
   static constexpr int BAR_OFF = STAGES * (A_BYTES + B_BYTES);
   static constexpr int NBARS = 2 * STAGES + 5;  // full[S], empty[S], tfull[2], tempty[2], drain
   static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;
-  static constexpr int BYTES = MISC_OFF + 16;
+  static constexpr int SCHED_OFF = (MISC_OFF + 16 + 15) / 16 * 16;  // tile schedule (tile_sched.cuh)
+  static constexpr int BYTES = SCHED_OFF + SchedSmem::BYTES;
   static constexpr int ALLOC = BYTES + 1024;  // dynamic smem requested (1024-byte alignment slack)
   static constexpr int TMEM_COLS = 2 * BN;
   static_assert(A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "tiles must stay 1024-byte aligned");
@@ -189,6 +193,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t drain_bar = bar0 + 8u * (2 * STAGES + 4);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::MISC_OFF);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::MISC_OFF + 4);
+  const Sched sched{sbase + L::SCHED_OFF, abort_flag, a.status, a.wait_limit_ns};
+  const long long first_unit = blockIdx.x;  // one CTA per unit; later units come from the schedule
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -200,6 +206,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mbar_init(tempty_bar(acc), 128);
     }
     ptx::mbar_init(drain_bar, 1);
+    sched.init(1 + 4);  // consumers: the MMA lane, the four epilogue warps
     *abort_flag = 0;
     ptx::fence_mbar_init();
   }
@@ -225,7 +232,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       uint32_t filled = 0, fill_parity = 0;  // per stage: ever filled / parity of the last fill
       bool ok = true;
-      for (long long unit = blockIdx.x; unit < a.units && ok; unit += gridDim.x) {
+      SchedOwner owner;
+      for (long long unit = first_unit; ok && unit >= 0;) {
+        owner.request(sched);  // the next unit, answered while this one loads
         const Unit u = decode_unit<BN>(a, unit);
         const int za = a.a_batched ? u.b : 0, zb = a.b_batched ? u.b : 0;
         for (int i = 0; i < u.nkb; ++i) {
@@ -256,9 +265,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             phase ^= 1u;
           }
         }
+        if (!ok) break;
+        ok = owner.publish_next(sched, 1, false, &unit, kStatusTimeoutProducer);
       }
-      // Teardown: every copy this CTA issued has landed before shared memory
-      // is released (immediate on the normal path: the MMA warp consumed them).
+      // Teardown: every copy this CTA issued (and a schedule request still in
+      // flight) has landed before shared memory is released (immediate on
+      // the normal path: the MMA warp consumed them).
+      owner.drain(sched);
       for (int s = 0; s < STAGES; ++s)
         if (filled & (1u << s))
           if (!ptx::mbar_wait_teardown(full_bar(s), (fill_parity >> s) & 1u, a.wait_limit_ns) && a.status)
@@ -280,7 +293,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (long long unit = blockIdx.x; unit < a.units && ok; unit += gridDim.x) {
+      int seq = 0;
+      for (long long unit = first_unit; ok && unit >= 0;) {
         const Unit u = decode_unit<BN>(a, unit);
         ok = ptx::mbar_wait_bounded(tempty_bar(acc), acc_phase ^ 1u, abort_flag, a.status, kStatusTimeoutMma,
                                     a.wait_limit_ns);
@@ -310,6 +324,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::umma_commit(tfull_bar(acc));  // accumulator complete
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1u;
+        ok = sched_take(sched, seq, false, &unit, kStatusTimeoutMma);
       }
     }
     __syncwarp();
@@ -319,7 +334,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row_in_tile = quarter * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (long long unit = blockIdx.x; unit < a.units; unit += gridDim.x) {
+    int seq = 0;
+    for (long long unit = first_unit; unit >= 0;) {
       const Unit u = decode_unit<BN>(a, unit);
       bool ok = true;
       if (lane == 0)
@@ -342,6 +358,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mbar_arrive(tempty_bar(acc));
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
+      long long next = -1;
+      if (lane == 0) ok = sched_take(sched, seq, false, &next, kStatusTimeoutEpilogue);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      unit = __shfl_sync(0xffffffffu, next, 0);
     }
     if constexpr (EPI == kEpiPeers) __threadfence_system();  // peer stores complete before the kernel ends
   }
