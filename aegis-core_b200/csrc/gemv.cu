@@ -7,9 +7,12 @@
 //     (split-K). LPR = BN/8 lanes cover one B row with 16-byte loads (8
 //     elements each), so a warp reads 32/LPR rows x BN*2 contiguous bytes per
 //     load instruction; the RG = 256/LPR row groups stride down the slice.
-//     U independent 16-byte loads per thread are in flight before any math.
-//   - A's rows for a batch are staged in shared memory as FP32 [k][MT] while
-//     the batch's weight loads are in flight, and read as broadcasts.
+//     U independent 16-byte loads per thread are in flight before any math,
+//     and the main loop has no barrier: each warp streams on its own.
+//   - The grid is sized to about four CTAs per SM (one wave); each CTA walks
+//     its K slice in batches of RG*U rows.
+//   - A's rows for the CTA's K slice are staged once in shared memory as FP32
+//     [k][MT] and read as broadcasts.
 //   - FP32 FMA into MT x 8 accumulators per thread, k ascending.
 //   - Reduction: row groups inside a warp by a fixed shuffle-xor tree, then
 //     the 8 warps through shared memory in warp order 0..7.
@@ -25,6 +28,7 @@
 #include "common.cuh"
 #include "device.h"
 #include "kernels.h"
+#include "ptx.cuh"
 #include "workspace.h"
 
 namespace aegis {
@@ -41,8 +45,11 @@ constexpr int kSmemFloats = 8192;  // 32 KiB: A chunk, then the cross-warp reduc
 // Rows per thread per batch (= independent 16-byte weight loads in flight):
 // bounded by the registers the MT x 8 accumulators leave.
 __host__ __device__ constexpr int gemv_rows_per_thread(int MT) {
-  return MT <= 2 ? 16 : (MT == 4 ? 8 : (MT == 8 ? 4 : 2));
+  return MT <= 2 ? 8 : (MT == 4 ? 4 : (MT == 8 ? 4 : 2));
 }
+// Resident CTAs per SM each instantiation is compiled for (its register
+// budget: four CTAs of 256 threads leave 64 registers a thread).
+__host__ __device__ constexpr int gemv_ctas_per_sm(int MT) { return MT <= 4 ? 4 : (MT == 8 ? 2 : 1); }
 
 struct GemvArgs {
   const void* A;
@@ -81,13 +88,12 @@ __device__ __forceinline__ void unpack8(const uint4& v, float (&b)[8]) {
 // VECB: B row-major with 16-byte-aligned rows (base, ldb); otherwise element loads
 // (row- or column-major B, any alignment).
 template <class T, int LPR, int MT, bool VECB>
-__global__ void __launch_bounds__(GThreads) gemv_kernel(GemvArgs a) {
+__global__ void __launch_bounds__(GThreads, gemv_ctas_per_sm(MT)) gemv_kernel(GemvArgs a) {
   using E = Elem<T>;
   constexpr int BN = 8 * LPR;
   constexpr int RG = GThreads / LPR;
   constexpr int U = gemv_rows_per_thread(MT);            // 16-byte loads in flight per thread
   static_assert(8 * MT * BN <= kSmemFloats, "cross-warp reduction must fit the shared buffer");
-  static_assert(RG * U * MT <= kSmemFloats, "a batch of A rows must fit the shared buffer");
   __shared__ __align__(16) float sm[kSmemFloats];
   __shared__ int s_last;
 
@@ -111,16 +117,23 @@ __global__ void __launch_bounds__(GThreads) gemv_kernel(GemvArgs a) {
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[m][j] = 0.f;
 
-  // Batches of U rows per thread (RG*U rows per CTA). All U weight loads of a
-  // batch are issued first; A's rows for the batch are staged into shared
-  // memory while they are in flight. The planner sizes a split to one batch.
-  for (int base = k_begin; base < k_end; base += RG * U) {
-    uint4 bv[U];
+  // Programmatic dependent launch: nothing global is read before the grids
+  // this one depends on have completed (their writes are then visible).
+  ptx::griddep_wait();
+
+  // This CTA's A rows, staged as FP32 [k][MT] in chunks of the shared buffer
+  // (one chunk for every plan the planner makes unless M and the split are
+  // both large); each chunk's weights stream in batches of U rows per
+  // thread: all U loads of a batch are issued before any of its math, and no
+  // barrier sits inside the batch loop, so the warps of the CTA (and the
+  // other CTAs on the SM) keep loads in flight while one warp computes.
+  constexpr int CH = (kSmemFloats / MT) / RG * RG;  // rows per chunk
+  auto load_batch = [&](uint4 (&bv)[U], int base, int c1) {
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int k = base + g + u * RG;
+      const int k = base + u * RG;
       bv[u] = make_uint4(0u, 0u, 0u, 0u);
-      if (k < k_end && ncols > 0) {
+      if (k < c1 && ncols > 0) {
         const long long gk = k;
         if constexpr (VECB) {
           const T* src = B + gk * a.ldb + n;
@@ -143,26 +156,43 @@ __global__ void __launch_bounds__(GThreads) gemv_kernel(GemvArgs a) {
         }
       }
     }
-    const int blen = min(RG * U, k_end - base);
-    __syncthreads();  // the previous batch's A rows are consumed
-    for (int i = tid; i < blen * MT; i += GThreads) {
+  };
+  bool released = false;
+  for (int c0 = k_begin; c0 < k_end; c0 += CH) {
+    const int c1 = min(k_end, c0 + CH);
+    uint4 bv[U];
+    // The chunk's first batch of weights is requested before its A rows are
+    // staged, so the two global latencies overlap.
+    load_batch(bv, c0 + g, c1);
+    if (c0 != k_begin) __syncthreads();  // the previous chunk's A rows are consumed
+    for (int i = tid; i < (c1 - c0) * MT; i += GThreads) {
       const int kk = i / MT, m = i % MT;
-      const int gm = m0 + m, gk = base + kk;
+      const int gm = m0 + m, gk = c0 + kk;
       float v = 0.f;
       if (gm < a.M) v = E::to_f32(a.ra ? A[(long long)gm * a.lda + gk] : A[gm + (long long)gk * a.lda]);
       sm[kk * MT + m] = v;
     }
     __syncthreads();
+    if (!released) {
+      // The next grid on the stream may launch and run up to its own
+      // griddepcontrol.wait while this one streams its weights.
+      ptx::griddep_launch_dependents();
+      released = true;
+    }
+    for (int base = c0 + g; base < c1; base += RG * U) {
+      if (base != c0 + g) load_batch(bv, base, c1);
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int kk = g + u * RG;
-      if (kk < blen) {
-        float bf[8];
-        unpack8<T>(bv[u], bf);
-        fma8<MT>(acc, bf, &sm[kk * MT]);
+      for (int u = 0; u < U; ++u) {
+        const int k = base + u * RG;
+        if (k < c1) {
+          float bf[8];
+          unpack8<T>(bv[u], bf);
+          fma8<MT>(acc, bf, &sm[(k - c0) * MT]);
+        }
       }
     }
   }
+  if (!released) ptx::griddep_launch_dependents();
 
   // Row groups inside the warp: fixed shuffle-xor tree over the lane bits above LPR.
 #pragma unroll
@@ -261,25 +291,23 @@ GPlan plan_for(int cfg, const GemmParams& p) {
   pl.tiles_m = ceil_div(p.M, pl.MT);
   pl.tiles = (long long)pl.tiles_n * pl.tiles_m * p.batch;
   const hw::DeviceLimits* d = hw::current();
-  const int sms = d ? d->sm_count : 0;
-  // One batch per thread per split: kc = RG * U rows (a split's weights are
-  // all in flight at once); the partials stay within the workspace cap.
-  const int RG = 256 / pl.LPR;
-  int kc = RG * gemv_rows_per_thread(pl.MT);
+  const int sms = d ? d->sm_count : 148;
+  // Split K so that tiles x splits fills one wave (gemv_ctas_per_sm CTAs per
+  // SM: ~128 KB of weight loads in flight per SM at MT <= 2), with at least
+  // 64 rows a split; a split's A rows should fit the shared buffer (kc * MT
+  // floats: one staging chunk), and the partials the workspace cap.
+  const long long target = (long long)sms * gemv_ctas_per_sm(pl.MT);
+  long long S = std::max<long long>(1, target / pl.tiles);  // rounded down: never a second wave
+  S = std::min<long long>(S, std::max(1, ceil_div(p.K, 64)));
+  int kc = ceil_div(ceil_div(p.K, int(S)), 16) * 16;
+  kc = std::min(kc, (kSmemFloats / pl.MT) / 16 * 16);
   const long long slot = pl.tiles * pl.MT * c.BN * (long long)sizeof(float);
   const long long cap = std::max<long long>(1, gemm::kSplitKMaxWorkspace / std::max<long long>(1, slot));
-  int S = ceil_div(p.K, kc);
-  if (S > cap) {
-    S = int(cap);
-    kc = ceil_div(ceil_div(p.K, S), 16) * 16;
-    S = ceil_div(p.K, kc);
+  if (ceil_div(p.K, kc) > cap) {
+    // Fewer, longer splits: only reachable when the shared buffer allows it.
+    kc = ceil_div(ceil_div(p.K, int(cap)), 16) * 16;
   }
-  if (S <= 1) {
-    S = 1;
-    kc = p.K;
-  }
-  (void)hw::current();
-  pl.S = S;
+  pl.S = ceil_div(p.K, kc);
   pl.kc = kc;
   return pl;
 }
@@ -289,10 +317,23 @@ bool vec_b_ok(const GemmParams& p) {
          (p.batch <= 1 || p.stride_b % 8 == 0);
 }
 
+// Launched with programmatic stream serialization: the grid may start while
+// the previous grid on the stream drains; it waits (griddepcontrol.wait)
+// before its first global read and lets its own dependents launch once its
+// weight loads are in flight.
 template <class T, int LPR, int MT, bool VECB>
 cudaError_t launch_t(const GemvArgs& a, dim3 grid, cudaStream_t s) {
-  gemv_kernel<T, LPR, MT, VECB><<<grid, GThreads, 0, s>>>(a);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(GThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, &gemv_kernel<T, LPR, MT, VECB>, a);
 }
 
 template <class T, int LPR, bool VECB>
@@ -472,8 +513,8 @@ cudaError_t gemv_run_noalloc(const GemmParams& p, cudaStream_t stream, const cha
     const int s_fit = int(std::max<long long>(1, (long long)kNoAllocPartialBytes / slot_bytes));
     pl.kc = ceil_div(ceil_div(p.K, s_fit), 16) * 16;
     pl.S = ceil_div(p.K, pl.kc);
-    if (pl.S == 1) pl.kc = p.K;
   }
+
   if (pl.tiles * (long long)sizeof(unsigned) > (long long)kNoAllocCounterBytes) {
     *why = "too many output tiles for the fixed ticket array";
     return cudaErrorInvalidValue;

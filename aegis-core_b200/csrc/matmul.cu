@@ -61,11 +61,13 @@ namespace detail {
 
 const gemm::KernelEntry* rule_for(const gemm::GemmParams& p, const gemm::DeviceCaps& caps) {
   if (p.M <= 16) {
-    // Decode: the tensor-core stream (ummav) measured faster than the CUDA-core
-    // GEMV at every BASELINE decode shape; it takes row-major operands the TMA
-    // path can address, the CUDA-core GEMV everything else.
+    // Decode. M <= 2: the CUDA-core weight stream (gemv_256x256_ksm) measured
+    // fastest at M = 1 on every BASELINE decode shape. From M = 4 the FP32 FMA
+    // work (M per weight element) makes the tensor-core stream (ummav) faster;
+    // it takes row-major operands the TMA path can address, the CUDA-core GEMV
+    // everything else.
+    if (p.M <= 2) return by_name("gemv_256x256_ksm");
     if (caps.arch == 100 && ummav_applicable(p)) return by_name("ummav_128x16x64_s6x2");
-    if (p.M <= 4) return by_name("gemv_128x256_ksm");
     if (p.M <= 8) return by_name("gemv_128x256_ksm");
     return by_name("gemv_64x256_ksm");
   }

@@ -9,10 +9,12 @@
 //   2. else the winner with the same N and K whose M is nearest in log2 (ties
 //      go to the larger M);
 //   3. else a built-in rule over this library's own kernels (there is no
-//      vendor-library dispatch target): M <= 16 -> the tensor-core decode
-//      stream (ummav) for row-major operands the TMA path can address, else
-//      the CUDA-core gemv; larger M with TMA-addressable operands -> umma
-//      (split-K when the tiles cannot fill the SMs); otherwise the simt kernel.
+//      vendor-library dispatch target): M <= 2 -> the CUDA-core decode GEMV;
+//      M <= 16 -> the tensor-core decode stream (ummav) for row-major
+//      operands the TMA path can address, else the CUDA-core GEMV; larger M
+//      with TMA-addressable operands -> umma (CTA pairs when M and N exceed
+//      128; split-K when the tiles cannot fill the SMs); otherwise the simt
+//      kernel.
 // Rows whose kernel the device cannot run (gemm::supported) are skipped.
 // alpha == 0 runs the scale-C kernel (C = beta * C; beta == 0 writes zeros
 // without reading C), as BLAS does.
