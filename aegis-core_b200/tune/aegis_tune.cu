@@ -1,0 +1,522 @@
+// aegis_tune: brute-force autotuner over the kernel registry, one process.
+//
+//   aegis_tune --shapes FILE [--dtype f16|bf16] [--prefix umma_,gemv_,ummav_]
+//              [--reps 20] [--warmup 3] [--seed S] [--data-seed 42]
+//              [--pairs 30] [--no-paired] [--window-ms 1.0]
+//
+// Follows the reference's tools/aegis_tune.cu (and its timing protocol v2,
+// src/bench/harness.cu:274-473) on this library's C ABI:
+//   - shapes: "M N K" per line, '#' comments;
+//   - per shape the problem is allocated once, in K = max(2, ceil(3 x L2 /
+//     footprint)) buffer sets rotated inside every timed window (cold L2);
+//   - the baseline (cuBLAS, FP32 compute, cublasGemmEx) and every registered
+//     configuration whose name starts with one of the prefixes run in an
+//     order shuffled per shape (seeded; the seed is printed);
+//   - each configuration: one untimed run checked against cuBLAS with the
+//     north-star bound max|C - C_ref| <= 2^-10 * K * max|A| * max|B| (a
+//     configuration that errors or fails is listed on stderr and not timed),
+//     then `reps` timed windows, each a CUDA graph of batch_n launches sized
+//     to >= window-ms, timed with events on the stream;
+//   - paired tie test: the fastest configuration against the runner-up and
+//     against cuBLAS over `pairs` alternating windows (a, b, a, b, ...); the
+//     95% percentile-bootstrap CI (2000 resamples, seeded) of the median of
+//     the per-pair ratios b / a.
+// stdout: JSON lines. {"kind":"run",...} once; {"kind":"measurement",...} per
+// timed configuration (the baseline has impl "cublas"); {"kind":"paired",...}
+// per tie test. aegis_perf.py ingests them into the perf DB and emits
+// include/aegis/winners/sm_100a.h.
+#include <cublas_v2.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <ctime>
+#include <fstream>
+#include <random>
+#include <sstream>
+#include <string>
+#include <vector>
+
+#include "aegis.h"
+
+namespace {
+
+#define CK(x)                                                                                         \
+  do {                                                                                                \
+    const cudaError_t e_ = (x);                                                                       \
+    if (e_ != cudaSuccess) {                                                                          \
+      std::fprintf(stderr, "aegis_tune: %s failed: %s (line %d)\n", #x, cudaGetErrorString(e_), __LINE__); \
+      std::exit(1);                                                                                   \
+    }                                                                                                 \
+  } while (0)
+
+struct Args {
+  std::string shapes;
+  int dtype = AEGIS_DTYPE_BF16;
+  std::vector<std::string> prefixes = {"umma_", "gemv_", "ummav_"};
+  int reps = 20, warmup = 3, pairs = 30;
+  unsigned long long seed = 0;
+  bool seed_given = false;
+  unsigned data_seed = 42;
+  bool paired = true;
+  double window_ms = 1.0;
+};
+
+std::vector<std::string> split(const std::string& s, char sep) {
+  std::vector<std::string> out;
+  std::stringstream ss(s);
+  for (std::string item; std::getline(ss, item, sep);)
+    if (!item.empty()) out.push_back(item);
+  return out;
+}
+
+[[noreturn]] void usage(const char* why) {
+  std::fprintf(stderr,
+               "aegis_tune: %s\nusage: aegis_tune --shapes FILE [--dtype f16|bf16] [--prefix a_,b_] [--reps N] "
+               "[--warmup N] [--seed S] [--data-seed S] [--pairs N] [--no-paired] [--window-ms X]\n",
+               why);
+  std::exit(2);
+}
+
+Args parse(int argc, char** argv) {
+  Args a;
+  for (int i = 1; i < argc; ++i) {
+    const std::string k = argv[i];
+    auto next = [&]() -> std::string {
+      if (i + 1 >= argc) usage(("missing value for " + k).c_str());
+      return argv[++i];
+    };
+    if (k == "--shapes") a.shapes = next();
+    else if (k == "--dtype") {
+      const std::string d = next();
+      if (d == "f16") a.dtype = AEGIS_DTYPE_F16;
+      else if (d == "bf16") a.dtype = AEGIS_DTYPE_BF16;
+      else usage("--dtype is f16 or bf16");
+    } else if (k == "--prefix") a.prefixes = split(next(), ',');
+    else if (k == "--reps") a.reps = std::stoi(next());
+    else if (k == "--warmup") a.warmup = std::stoi(next());
+    else if (k == "--pairs") a.pairs = std::stoi(next());
+    else if (k == "--seed") { a.seed = std::stoull(next()); a.seed_given = true; }
+    else if (k == "--data-seed") a.data_seed = unsigned(std::stoul(next()));
+    else if (k == "--no-paired") a.paired = false;
+    else if (k == "--window-ms") a.window_ms = std::stod(next());
+    else usage(("unknown argument " + k).c_str());
+  }
+  if (a.shapes.empty()) usage("--shapes is required");
+  if (a.reps < 3 || a.warmup < 1 || a.pairs < 5) usage("--reps >= 3, --warmup >= 1, --pairs >= 5");
+  if (!a.seed_given) a.seed = (unsigned long long)std::chrono::steady_clock::now().time_since_epoch().count();
+  return a;
+}
+
+struct Shape { int M, N, K; };
+
+std::vector<Shape> read_shapes(const std::string& path) {
+  std::ifstream f(path);
+  if (!f) usage(("cannot read " + path).c_str());
+  std::vector<Shape> out;
+  for (std::string line; std::getline(f, line);) {
+    const size_t h = line.find('#');
+    if (h != std::string::npos) line.resize(h);
+    std::stringstream ss(line);
+    Shape s{};
+    if (ss >> s.M >> s.N >> s.K) {
+      if (s.M <= 0 || s.N <= 0 || s.K <= 0) usage("shape sizes must be positive");
+      out.push_back(s);
+    }
+  }
+  return out;
+}
+
+// Registry names with their config JSON and tune_max_m, from
+// aegis_registry_json (a flat array of flat objects with one nested
+// "config" object).
+struct Kernel { std::string name, config; int tune_max_m = 0; bool supported = false; };
+
+std::string field(const std::string& obj, const std::string& key) {
+  const std::string k = "\"" + key + "\":";
+  const size_t p = obj.find(k);
+  if (p == std::string::npos) return "";
+  size_t b = p + k.size(), e = b;
+  if (obj[b] == '"') {
+    e = obj.find('"', b + 1);
+    return obj.substr(b + 1, e - b - 1);
+  }
+  if (obj[b] == '{') {
+    int depth = 0;
+    for (e = b; e < obj.size(); ++e) {
+      if (obj[e] == '{') ++depth;
+      if (obj[e] == '}' && --depth == 0) break;
+    }
+    return obj.substr(b, e - b + 1);
+  }
+  while (e < obj.size() && obj[e] != ',' && obj[e] != '}') ++e;
+  return obj.substr(b, e - b);
+}
+
+std::vector<Kernel> registry(aegis_context* ctx) {
+  size_t need = 0;
+  if (aegis_registry_json(ctx, nullptr, 0, &need) != AEGIS_OK) usage(aegis_last_error_string());
+  std::string j(need, '\0');
+  if (aegis_registry_json(ctx, j.data(), j.size(), &need) != AEGIS_OK) usage(aegis_last_error_string());
+  j.resize(std::strlen(j.c_str()));
+  std::vector<Kernel> out;
+  // Split on top-level objects.
+  int depth = 0;
+  size_t start = 0;
+  for (size_t i = 0; i < j.size(); ++i) {
+    if (j[i] == '{' && depth++ == 0) start = i;
+    if (j[i] == '}' && --depth == 0) {
+      const std::string o = j.substr(start, i - start + 1);
+      Kernel k;
+      k.name = field(o, "name");
+      k.config = field(o, "config");
+      k.tune_max_m = std::atoi(field(o, "tune_max_m").c_str());
+      k.supported = field(o, "supported") == "true";
+      out.push_back(k);
+    }
+  }
+  return out;
+}
+
+// Seeded uniform[-1, 1] fill (counter-based hash: the data depend only on
+// the seed and the index).
+__global__ void fill_kernel(uint16_t* p, long long n, unsigned seed, int bf16) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    unsigned long long z = (unsigned long long)i * 0x9E3779B97F4A7C15ull + seed * 0xD1B54A32D192ED03ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    z ^= z >> 31;
+    const float u = float(z >> 40) * (2.0f / 16777216.0f) - 1.0f;
+    if (bf16) {
+      const __nv_bfloat16 h = __float2bfloat16_rn(u);
+      p[i] = *reinterpret_cast<const uint16_t*>(&h);
+    } else {
+      const __half h = __float2half_rn(u);
+      p[i] = *reinterpret_cast<const uint16_t*>(&h);
+    }
+  }
+}
+
+// max |x - y| over two 16-bit matrices, as float, into out (one atomicMax on
+// the float's bits: values are non-negative).
+__global__ void maxdiff_kernel(const uint16_t* x, const uint16_t* y, long long n, int bf16, unsigned* out) {
+  float m = 0.f;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    float a, b;
+    if (bf16) {
+      a = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(x + i));
+      b = __bfloat162float(*reinterpret_cast<const __nv_bfloat16*>(y + i));
+    } else {
+      a = __half2float(*reinterpret_cast<const __half*>(x + i));
+      b = __half2float(*reinterpret_cast<const __half*>(y + i));
+    }
+    const float d = fabsf(a - b);
+    m = (d != d) ? INFINITY : fmaxf(m, d);
+  }
+  atomicMax(out, __float_as_uint(m));
+}
+
+struct Problem {
+  int M, N, K, dtype, sets;
+  std::vector<uint16_t*> A, B, C;
+  uint16_t* C_ref = nullptr;
+};
+
+double median(std::vector<double> v) {
+  std::sort(v.begin(), v.end());
+  const size_t n = v.size();
+  return n % 2 ? v[n / 2] : 0.5 * (v[n / 2 - 1] + v[n / 2]);
+}
+double quantile(std::vector<double> v, double q) {
+  std::sort(v.begin(), v.end());
+  const double pos = q * double(v.size() - 1);
+  const size_t lo = size_t(pos);
+  const size_t hi = std::min(v.size() - 1, lo + 1);
+  return v[lo] + (v[hi] - v[lo]) * (pos - double(lo));
+}
+
+// 95% percentile-bootstrap CI of the median of `r`.
+void bootstrap_ci(const std::vector<double>& r, unsigned long long seed, int resamples, double* lo, double* hi) {
+  std::mt19937_64 g(seed);
+  std::uniform_int_distribution<size_t> pick(0, r.size() - 1);
+  std::vector<double> meds(resamples), s(r.size());
+  for (int b = 0; b < resamples; ++b) {
+    for (auto& x : s) x = r[pick(g)];
+    meds[b] = median(s);
+  }
+  *lo = quantile(meds, 0.025);
+  *hi = quantile(meds, 0.975);
+}
+
+class Tuner {
+ public:
+  Tuner(const Args& a) : a_(a) {
+    CK(cudaSetDevice(0));
+    CK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+    if (aegis_create(&ctx_, 0) != AEGIS_OK) usage(aegis_last_error_string());
+    if (aegis_set_stream(ctx_, stream_) != AEGIS_OK) usage(aegis_last_error_string());
+    if (cublasCreate(&blas_) != CUBLAS_STATUS_SUCCESS) usage("cublasCreate failed");
+    cublasSetStream(blas_, stream_);
+    cublasSetMathMode(blas_, CUBLAS_DEFAULT_MATH);
+    CK(cudaEventCreate(&e0_));
+    CK(cudaEventCreate(&e1_));
+    CK(cudaMalloc(&maxdiff_, sizeof(unsigned)));
+    CK(cudaGetDeviceProperties(&prop_, 0));
+  }
+  ~Tuner() {
+    cublasDestroy(blas_);
+    aegis_destroy(ctx_);
+    cudaStreamDestroy(stream_);
+  }
+
+  void run(const std::vector<Shape>& shapes) {
+    char run_id[64];
+    std::snprintf(run_id, sizeof run_id, "tune-%llx", a_.seed);
+    run_id_ = run_id;
+    int drv = 0, rt = 0;
+    cudaDriverGetVersion(&drv);
+    cudaRuntimeGetVersion(&rt);
+    char when[32];
+    const std::time_t t = std::time(nullptr);
+    std::strftime(when, sizeof when, "%Y-%m-%dT%H:%M:%SZ", std::gmtime(&t));
+    std::printf("{\"kind\":\"run\",\"run_id\":\"%s\",\"device\":\"%s\",\"sm_arch\":%d,\"sms\":%d,\"cuda_ver\":%d,"
+                "\"driver_ver\":%d,\"started_at\":\"%s\",\"seed\":%llu,\"data_seed\":%u,\"dtype\":\"%s\","
+                "\"protocol_version\":2}\n",
+                run_id, prop_.name, prop_.major * 10 + prop_.minor, prop_.multiProcessorCount, rt, drv, when, a_.seed,
+                a_.data_seed, dname());
+    std::fflush(stdout);
+    kernels_ = registry(ctx_);
+    for (size_t si = 0; si < shapes.size(); ++si) tune_shape(shapes[si], si);
+  }
+
+ private:
+  const char* dname() const { return a_.dtype == AEGIS_DTYPE_BF16 ? "bf16" : "f16"; }
+
+  Problem make(const Shape& s) {
+    Problem p{s.M, s.N, s.K, a_.dtype, 0, {}, {}, {}, nullptr};
+    const double footprint = 2.0 * (double(s.M) * s.K + double(s.K) * s.N + double(s.M) * s.N);
+    const double l2 = double(prop_.l2CacheSize > 0 ? prop_.l2CacheSize : 126 << 20);
+    p.sets = std::max(2, int(std::ceil(3.0 * l2 / footprint)));
+    const int bf = a_.dtype == AEGIS_DTYPE_BF16;
+    for (int i = 0; i < p.sets; ++i) {
+      uint16_t *A, *B, *C;
+      CK(cudaMalloc(&A, size_t(s.M) * s.K * 2));
+      CK(cudaMalloc(&B, size_t(s.K) * s.N * 2));
+      CK(cudaMalloc(&C, size_t(s.M) * s.N * 2));
+      // Every set holds the same data (seeded), so any set checks the same.
+      fill_kernel<<<1024, 256, 0, stream_>>>(A, (long long)s.M * s.K, a_.data_seed * 2u + 0u, bf);
+      fill_kernel<<<1024, 256, 0, stream_>>>(B, (long long)s.K * s.N, a_.data_seed * 2u + 1u, bf);
+      CK(cudaMemsetAsync(C, 0, size_t(s.M) * s.N * 2, stream_));
+      p.A.push_back(A);
+      p.B.push_back(B);
+      p.C.push_back(C);
+    }
+    CK(cudaMalloc(&p.C_ref, size_t(s.M) * s.N * 2));
+    CK(cudaStreamSynchronize(stream_));
+    return p;
+  }
+  void release(Problem& p) {
+    for (int i = 0; i < p.sets; ++i) {
+      cudaFree(p.A[i]);
+      cudaFree(p.B[i]);
+      cudaFree(p.C[i]);
+    }
+    cudaFree(p.C_ref);
+  }
+
+  // One launch of `impl` ("cublas" = the baseline) on buffer set i; C row-major.
+  bool launch(const Problem& p, const std::string& impl, int i, uint16_t* C) {
+    if (impl == "cublas") {
+      // Row-major C = A*B is column-major C^T = B^T * A^T.
+      const float one = 1.f, zero = 0.f;
+      const cudaDataType t = a_.dtype == AEGIS_DTYPE_BF16 ? CUDA_R_16BF : CUDA_R_16F;
+      return cublasGemmEx(blas_, CUBLAS_OP_N, CUBLAS_OP_N, p.N, p.M, p.K, &one, p.B[i], t, p.N, p.A[i], t, p.K, &zero,
+                          C, t, p.N, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT) == CUBLAS_STATUS_SUCCESS;
+    }
+    return aegis_gemm_impl(ctx_, impl.c_str(), a_.dtype, AEGIS_ROW_MAJOR, AEGIS_ROW_MAJOR, p.M, p.N, p.K, 1.f, p.A[i],
+                           p.K, 0, p.B[i], p.N, 0, 0.f, C, p.N, 0, 1) == AEGIS_OK;
+  }
+
+  float max_abs_diff(const Problem& p, const uint16_t* C) {
+    CK(cudaMemsetAsync(maxdiff_, 0, sizeof(unsigned), stream_));
+    maxdiff_kernel<<<1024, 256, 0, stream_>>>(C, p.C_ref, (long long)p.M * p.N, a_.dtype == AEGIS_DTYPE_BF16,
+                                              maxdiff_);
+    unsigned bits = 0;
+    CK(cudaMemcpyAsync(&bits, maxdiff_, sizeof bits, cudaMemcpyDeviceToHost, stream_));
+    CK(cudaStreamSynchronize(stream_));
+    float f;
+    std::memcpy(&f, &bits, sizeof f);
+    return f;
+  }
+
+  // Per-launch microseconds of windows of `batch` graph-captured launches
+  // rotating the buffer sets; `reps` windows.
+  cudaGraphExec_t capture(const Problem& p, const std::string& impl, int batch) {
+    cudaGraph_t g;
+    CK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+    for (int j = 0; j < batch; ++j) launch(p, impl, j % p.sets, p.C[j % p.sets]);
+    CK(cudaStreamEndCapture(stream_, &g));
+    cudaGraphExec_t ge;
+    CK(cudaGraphInstantiate(&ge, g, 0));
+    CK(cudaGraphDestroy(g));
+    return ge;
+  }
+  double time_window(cudaGraphExec_t ge, int batch) {
+    CK(cudaEventRecord(e0_, stream_));
+    CK(cudaGraphLaunch(ge, stream_));
+    CK(cudaEventRecord(e1_, stream_));
+    CK(cudaEventSynchronize(e1_));
+    float ms = 0.f;
+    CK(cudaEventElapsedTime(&ms, e0_, e1_));
+    return double(ms) * 1e3 / batch;
+  }
+  int calibrate(const Problem& p, const std::string& impl) {
+    int batch = 1;
+    for (;;) {
+      cudaGraphExec_t ge = capture(p, impl, batch);
+      CK(cudaGraphLaunch(ge, stream_));  // warm
+      const double us = time_window(ge, batch);
+      cudaGraphExecDestroy(ge);
+      if (us * batch >= a_.window_ms * 1e3 || batch >= 4096) return batch;
+      batch = std::min(4096, std::max(batch * 2, int(std::ceil(a_.window_ms * 1e3 / std::max(us, 0.5)))));
+    }
+  }
+
+  struct Result { std::string impl, config; double med, p10, p90; int batch; float err; };
+
+  void tune_shape(const Shape& s, size_t shape_index) {
+    Problem p = make(s);
+    const double tol = std::ldexp(1.0, -10) * s.K;  // max|A| = max|B| = 1 (uniform[-1, 1])
+    // Reference result (cuBLAS) into C_ref.
+    if (!launch(p, "cublas", 0, p.C_ref)) usage("cuBLAS failed on a tuning shape");
+    CK(cudaStreamSynchronize(stream_));
+
+    std::vector<std::string> order = {"cublas"};
+    std::vector<std::string> configs;
+    for (const Kernel& k : kernels_) {
+      if (!k.supported) continue;
+      if (k.tune_max_m > 0 && s.M > k.tune_max_m) continue;
+      bool match = false;
+      for (const auto& pre : a_.prefixes) match |= k.name.rfind(pre, 0) == 0;
+      if (match) order.push_back(k.name);
+    }
+    const unsigned long long shape_seed = a_.seed ^ (0x9E3779B97F4A7C15ull * (shape_index + 1));
+    std::mt19937_64 g(shape_seed);
+    std::shuffle(order.begin(), order.end(), g);
+
+    std::vector<Result> results;
+    for (size_t oi = 0; oi < order.size(); ++oi) {
+      const std::string& impl = order[oi];
+      // Untimed run + check.
+      CK(cudaMemsetAsync(p.C[0], 0xff, size_t(s.M) * s.N * 2, stream_));  // NaN poison
+      if (!launch(p, impl, 0, p.C[0]) || cudaStreamSynchronize(stream_) != cudaSuccess) {
+        std::fprintf(stderr, "aegis_tune: %dx%dx%d %s: launch failed (%s)\n", s.M, s.N, s.K, impl.c_str(),
+                     aegis_last_error_string());
+        cudaGetLastError();
+        continue;
+      }
+      const float err = impl == "cublas" ? 0.f : max_abs_diff(p, p.C[0]);
+      if (!(err <= tol)) {
+        std::fprintf(stderr, "aegis_tune: %dx%dx%d %s: check failed, max|C - C_cublas| = %g > %g\n", s.M, s.N, s.K,
+                     impl.c_str(), err, tol);
+        continue;
+      }
+      for (int w = 0; w < a_.warmup; ++w) launch(p, impl, w % p.sets, p.C[w % p.sets]);
+      const int batch = calibrate(p, impl);
+      cudaGraphExec_t ge = capture(p, impl, batch);
+      CK(cudaGraphLaunch(ge, stream_));
+      std::vector<double> us;
+      for (int r = 0; r < a_.reps; ++r) us.push_back(time_window(ge, batch));
+      cudaGraphExecDestroy(ge);
+      Result res{impl, config_of(impl), median(us), quantile(us, 0.1), quantile(us, 0.9), batch, err};
+      results.push_back(res);
+      const double flops = 2.0 * s.M * s.N * s.K;
+      const double bytes = 2.0 * (double(s.M) * s.K + double(s.K) * s.N + double(s.M) * s.N);
+      std::printf("{\"kind\":\"measurement\",\"run_id\":\"%s\",\"op\":\"gemm\",\"dtype\":\"%s\",\"m\":%d,\"n\":%d,"
+                  "\"k\":%d,\"impl\":\"%s\",\"config\":%s,\"median_us\":%.4f,\"p10_us\":%.4f,\"p90_us\":%.4f,"
+                  "\"tflops\":%.3f,\"gbps\":%.2f,\"weights_gbps\":%.2f,\"reps\":%d,\"batch_n\":%d,"
+                  "\"buffer_sets\":%d,\"cache_mode\":\"cold\",\"protocol_version\":2,\"checked\":%s,\"pass\":true,"
+                  "\"max_abs_err\":%.6g,\"tol\":%.6g,\"tune\":{\"seed\":%llu,\"shape_seed\":%llu,\"order\":%zu}}\n",
+                  run_id_.c_str(), dname(), s.M, s.N, s.K, impl.c_str(), res.config.c_str(), res.med, res.p10,
+                  res.p90, flops / (res.med * 1e6), bytes / (res.med * 1e3), 2.0 * s.K * s.N / (res.med * 1e3),
+                  a_.reps, batch, p.sets, impl == "cublas" ? "false" : "true", err, tol, a_.seed, shape_seed, oi);
+      std::fflush(stdout);
+    }
+
+    // Paired tie tests: fastest config vs runner-up and vs cuBLAS.
+    std::vector<const Result*> ours;
+    const Result* base = nullptr;
+    for (const Result& r : results) {
+      if (r.impl == "cublas")
+        base = &r;
+      else
+        ours.push_back(&r);
+    }
+    std::sort(ours.begin(), ours.end(), [](const Result* x, const Result* y) { return x->med < y->med; });
+    if (a_.paired && !ours.empty()) {
+      if (ours.size() > 1) paired(p, s, *ours[0], *ours[1], "runner_up", shape_seed);
+      if (base) paired(p, s, *ours[0], *base, "cublas", shape_seed + 1);
+    }
+    release(p);
+  }
+
+  std::string config_of(const std::string& impl) const {
+    if (impl == "cublas") return "{\"family\":\"cublas\",\"compute\":\"32F\"}";
+    for (const Kernel& k : kernels_)
+      if (k.name == impl) return k.config.empty() ? "{}" : k.config;
+    return "{}";
+  }
+
+  void paired(const Problem& p, const Shape& s, const Result& a, const Result& b, const char* role,
+              unsigned long long seed) {
+    const int batch = std::max(a.batch, b.batch);
+    cudaGraphExec_t ga = capture(p, a.impl, batch), gb = capture(p, b.impl, batch);
+    CK(cudaGraphLaunch(ga, stream_));
+    CK(cudaGraphLaunch(gb, stream_));
+    std::vector<double> ratio;
+    for (int i = 0; i < a_.pairs; ++i) {
+      const double ta = time_window(ga, batch);
+      const double tb = time_window(gb, batch);
+      ratio.push_back(tb / ta);
+    }
+    cudaGraphExecDestroy(ga);
+    cudaGraphExecDestroy(gb);
+    double lo = 0, hi = 0;
+    const int resamples = 2000;
+    bootstrap_ci(ratio, seed, resamples, &lo, &hi);
+    std::printf("{\"kind\":\"paired\",\"run_id\":\"%s\",\"op\":\"gemm\",\"dtype\":\"%s\",\"m\":%d,\"n\":%d,\"k\":%d,"
+                "\"a_impl\":\"%s\",\"b_impl\":\"%s\",\"role\":\"%s\",\"pairs\":%d,\"batch_n\":%d,"
+                "\"ratio_median\":%.5f,\"ratio_ci_lo\":%.5f,\"ratio_ci_hi\":%.5f,\"tied\":%s,"
+                "\"bootstrap_resamples\":%d,\"bootstrap_seed\":%llu,\"protocol_version\":2,\"cache_mode\":\"cold\"}\n",
+                run_id_.c_str(), dname(), s.M, s.N, s.K, a.impl.c_str(), b.impl.c_str(), role, a_.pairs, batch,
+                median(ratio), lo, hi, (lo <= 1.0 && hi >= 1.0) ? "true" : "false", resamples, seed);
+    std::fflush(stdout);
+  }
+
+  Args a_;
+  cudaStream_t stream_{};
+  aegis_context* ctx_ = nullptr;
+  cublasHandle_t blas_{};
+  cudaEvent_t e0_{}, e1_{};
+  unsigned* maxdiff_ = nullptr;
+  cudaDeviceProp prop_{};
+  std::vector<Kernel> kernels_;
+  std::string run_id_;
+};
+
+}  // namespace
+
+int main(int argc, char** argv) {
+  const Args a = parse(argc, argv);
+  const std::vector<Shape> shapes = read_shapes(a.shapes);
+  std::fprintf(stderr, "aegis_tune: %zu shapes, seed %llu\n", shapes.size(), a.seed);
+  Tuner t(a);
+  t.run(shapes);
+  return 0;
+}

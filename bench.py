@@ -77,7 +77,9 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi samples every 200 ms while the timed region runs."""
+    """nvidia-smi samples every 50 ms while the timed region runs. start()
+    returns once the first sample has arrived and stop() waits for one more,
+    so even a region shorter than the interval is bracketed by samples."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -90,13 +92,19 @@ class ClockSampler:
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200", "-i", str(self.device)], stdout=subprocess.PIPE,
+                                          "-lms", "50", "-i", str(self.device)], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
             return
         self.thread = threading.Thread(target=self._read, daemon=True)
         self.thread.start()
+        self._wait_for(1, 5.0)
+
+    def _wait_for(self, n, limit_s):
+        t0 = time.time()
+        while len(self.lines) < n and time.time() - t0 < limit_s and self.proc.poll() is None:
+            time.sleep(0.01)
 
     def _read(self):
         for line in self.proc.stdout:
@@ -105,7 +113,7 @@ class ClockSampler:
     def stop(self):
         if not self.proc:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        time.sleep(0.25)
+        self._wait_for(len(self.lines) + 1, 2.0)
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)

@@ -176,3 +176,36 @@ def test_watchdog_selftest_and_context_reuse(cuda):
     dA, dB, dC = dev(torch, A), dev(torch, B), dev(torch, np.zeros(256 * 256, np.uint16))
     run(torch, ctx, d, dA, dB, dC, "umma_128x256x64_s4")
     check(d, A, B, None, host(dC), op.gemm_ref(d, A, B))
+
+
+def _winner_rows():
+    """(M, N, K, impl) of every row of the committed winners header."""
+    import re
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "aegis", "winners",
+                        "sm_100a.h")
+    if not os.path.exists(path):
+        return []
+    pat = re.compile(r'^\s*\{(\d+), (\d+), (\d+), "([^"]+)", aegis::detail::Dispatch::Aegis')
+    return [(int(m[1]), int(m[2]), int(m[3]), m[4]) for m in map(pat.match, open(path)) if m]
+
+
+def test_dispatch_follows_the_tuned_winners(cuda):
+    """aegis::matmul picks the tuned winner for every shape of the compiled
+    header (exact match), and the nearest-M row for an untuned M of a tuned
+    (N, K) (reference matmul.cu:432-467; ties go to the larger M)."""
+    rows = _winner_rows()
+    if not rows:
+        pytest.skip("no winners header")
+    ctx = context(cuda)
+    for m, n, k, impl in rows:
+        assert ctx.choice(m, n, k) == impl, (m, n, k)
+    by_nk = {}
+    for m, n, k, impl in rows:
+        by_nk.setdefault((n, k), []).append((m, impl))
+    import math
+    for (n, k), ms in by_nk.items():
+        for q in (2, 3, 8, 64, 3000):
+            if any(m == q for m, _ in ms):
+                continue
+            best = min(ms, key=lambda r: (abs(math.log2(r[0]) - math.log2(q)), -r[0]))
+            assert ctx.choice(q, n, k) == best[1], (q, n, k)
