@@ -132,7 +132,8 @@ def gemm_ref_rows(d: Desc, A, B, r0: int, r1: int, C0=None, nthreads: int | None
 
 def tolerance(d: Desc, A, B, C0=None, c: float = 2.0, kind: str = "reference") -> float:
     """kind "reference": c*sqrt(K)*eps*max|A|*max|B|*|alpha| + eps*|beta|*max|C0|
-    (reference.cu:186-194); kind "north_star": 2^-10*K*max|A|*max|B|*|alpha| (+ beta term)."""
+    (reference.cu:186-194); kind "north_star": eps*K*max|A|*max|B|*|alpha| (+ beta term), eps = 2^-10
+    for f16 outputs (the bound as stated) and 2^-7 for bf16 outputs (the output type's eps)."""
     A, B, C0 = _u16(A), _u16(B), _u16(C0)
     return oracle_lib().oracle_tolerance(ctypes.byref(d), A.ctypes.data, A.size, B.ctypes.data, B.size,
                                          C0.ctypes.data if C0 is not None else None,

@@ -3,7 +3,8 @@ only the allocator), a C-ABI context bound to torch's current stream, and
 oracle comparisons with both tolerance forms the project uses:
   - the reference's bound c*sqrt(K)*eps*max|A|*max|B|*|alpha| + eps*|beta|*max|C0|
     (c = 2, src/bench/reference.cu:186-194), and
-  - the north-star bound 2^-10*K*max|A|*max|B|*|alpha| (+ the beta term)."""
+  - the north-star bound eps*K*max|A|*max|B|*|alpha| (+ the beta term), eps = 2^-10
+    for f16 outputs as stated, 2^-7 for bf16 outputs."""
 import numpy as np
 
 import aegis_capi as ac

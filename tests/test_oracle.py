@@ -150,3 +150,15 @@ def test_datagen_normal_distribution():
     assert abs(w.mean()) < 1e-3 and abs(w.std() - 0.02) < 1e-3
     g1, g2 = ac.Generator(9), ac.Generator(9)
     assert np.array_equal(g1.uniform(1000), g2.uniform(1000))
+
+
+def test_north_star_bound_scales_with_the_output_type():
+    """The north-star bound eps*K*max|A|*max|B| uses the output type's eps:
+    2^-10 for f16 (as stated) and 2^-7 for bf16, whose rounding alone can
+    exceed 2^-10*K*max|A|*max|B| at small K."""
+    g = ac.Generator(5)
+    for dtype, eps in (("f16", 2.0 ** -10), ("bf16", 2.0 ** -7)):
+        A, B = g.uniform(4 * 3, dtype, -4, 4), g.uniform(3 * 5, dtype, -4, 4)
+        d = op.make_desc(4, 5, 3, dtype=dtype)
+        ma, mb = np.abs(ac.to_f32(A, dtype)).max(), np.abs(ac.to_f32(B, dtype)).max()
+        assert op.tolerance(d, A, B, kind="north_star") == pytest.approx(eps * 3 * ma * mb, rel=1e-12)
