@@ -117,6 +117,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   ptx::cluster_sync();  // both CTAs' barriers exist before any remote arrive or copy
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Programmatic dependent launch: the prologue above (barriers, TMEM,
+  // descriptor prefetch) may overlap the previous grid on the stream; no
+  // thread touches global memory before that grid has completed, and the
+  // next grid may launch (its CTAs start as SMs free up).
+  ptx::griddep_wait();
+  ptx::griddep_launch_dependents();
 
   if (warp == 0) {
     // ------------------------------------------------ TMA producer (both CTAs)
@@ -129,7 +135,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       SchedOwner owner;  // used by the leader only
       int seq = 0;       // the peer's position in the schedule
       for (long long unit = first_unit; ok && unit >= 0;) {
-        if (rank == 0) owner.request(sched);  // the next unit, answered while this one loads
+        if (rank == 0 && a.steal) owner.request(sched);  // the next unit, answered while this one loads
         const Unit u = decode_unit_pair<BN>(a, unit);
         const int za = a.a_batched ? u.b : 0, zb = a.b_batched ? u.b : 0;
         const int my_m = u.m0 + 128 * int(rank), my_n = u.n0 + BNH * int(rank);

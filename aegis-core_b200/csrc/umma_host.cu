@@ -80,6 +80,10 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
                                                             int N, T* __restrict__ C, long long ldc,
                                                             long long stride_c, float alpha, float beta) {
   using E = Elem<T>;
+  // Launched as a programmatic dependent of the GEMM that wrote the partials:
+  // nothing is read before that grid has completed.
+  ptx::griddep_wait();
+  ptx::griddep_launch_dependents();
   const long long plane = (long long)batch * M * N;
   constexpr int W = VEC4 ? 4 : 1;
   const int nw = N / W;
@@ -126,13 +130,19 @@ cudaError_t launch_reduce(const float* part, int S, const GemmParams& p, cudaStr
   const long long total = (long long)p.batch * p.M * (vec ? p.N / 4 : p.N);
   const int blocks = int(std::max<long long>(1, std::min<long long>((total + 255) / 256, (long long)sms * 8)));
   T* C = static_cast<T*>(p.C);
-  if (vec)
-    splitk_reduce_kernel<T, true><<<blocks, 256, 0, s>>>(part, S, p.batch, p.M, p.N, C, p.ldc, p.stride_c, p.alpha,
-                                                          p.beta);
-  else
-    splitk_reduce_kernel<T, false><<<blocks, 256, 0, s>>>(part, S, p.batch, p.M, p.N, C, p.ldc, p.stride_c, p.alpha,
-                                                           p.beta);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(unsigned(blocks));
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return vec ? cudaLaunchKernelEx(&cfg, &splitk_reduce_kernel<T, true>, part, S, p.batch, p.M, p.N, C, p.ldc,
+                                  p.stride_c, p.alpha, p.beta)
+             : cudaLaunchKernelEx(&cfg, &splitk_reduce_kernel<T, false>, part, S, p.batch, p.M, p.N, C, p.ldc,
+                                  p.stride_c, p.alpha, p.beta);
 }
 
 // ---------------------------------------------------------------- planning
@@ -145,6 +155,7 @@ struct Plan {
   int splits = 1, kb_per_split = 0, kb_total = 0;
   int tiles_m = 0, tiles_n = 0;
   int group_m = umma::kGroupM;
+  bool steal = true;  // more units than resident CTAs (pairs)
   long long tiles = 0, units = 0;
   int grid = 0;
 };
@@ -229,6 +240,11 @@ Plan make_plan(int cfg, const GemmParams& p) {
   // One CTA (pair: one cluster of two) per unit: the CTAs that fit run and
   // take the rest in launch order (tile_sched.cuh).
   pl.grid = int(std::max<long long>(1, std::min<long long>(pl.units, kMaxUnits))) * c.CTAS;
+  // When every unit has a resident CTA (pair) from the start there is nothing
+  // to take: no cluster-launch-control request (its failed answer would only
+  // delay the CTAs' exit). If fewer CTAs turn out resident, the others still
+  // start later and run their own units.
+  pl.steal = sms <= 0 || pl.units > sms;
   return pl;
 }
 
@@ -243,6 +259,7 @@ umma::Args make_args(const GemmParams& p, const Plan& pl) {
   a.tiles_m = pl.tiles_m;
   a.tiles_n = pl.tiles_n;
   a.group_m = pl.group_m;
+  a.steal = pl.steal ? 1 : 0;
   a.splits = pl.splits;
   a.kb_per_split = pl.kb_per_split;
   a.kb_total = pl.kb_total;

@@ -59,6 +59,7 @@ struct Args {
   int a_batched, b_batched;  // use the batch coordinate for A / B loads
   int tiles_m, tiles_n;
   int group_m;      // tile rows per raster group (>= 1)
+  int steal;        // more units than resident CTAs (pairs): take the rest by cluster launch control
   int splits, kb_per_split, kb_total;
   long long units;  // batch * tiles_m * tiles_n * splits
   void* C;
@@ -222,6 +223,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Programmatic dependent launch: the prologue above (barriers, TMEM,
+  // descriptor prefetch) may overlap the previous grid on the stream; no
+  // thread touches global memory before that grid has completed, and the
+  // next grid may launch (its CTAs start as SMs free up).
+  ptx::griddep_wait();
+  ptx::griddep_launch_dependents();
 
   if (warp == 0) {
     // ------------------------------------------------ TMA producer
@@ -234,7 +241,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       SchedOwner owner;
       for (long long unit = first_unit; ok && unit >= 0;) {
-        owner.request(sched);  // the next unit, answered while this one loads
+        if (a.steal) owner.request(sched);  // the next unit, answered while this one loads
         const Unit u = decode_unit<BN>(a, unit);
         const int za = a.a_batched ? u.b : 0, zb = a.b_batched ? u.b : 0;
         for (int i = 0; i < u.nkb; ++i) {

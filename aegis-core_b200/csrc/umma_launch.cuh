@@ -24,8 +24,17 @@ cudaError_t launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const Args&
   static hw::PerDevice once;
   constexpr size_t smem = size_t(Layout<BN, STAGES>::ALLOC);
   if (const cudaError_t e = hw::configure_smem(once, kern, smem); e != cudaSuccess) return e;
-  kern<<<grid, kThreads, smem, stream>>>(ta, tb, a);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(unsigned(grid));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // the kernel waits (griddepcontrol.wait)
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, ta, tb, a);
 }
 
 template <class T, int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
@@ -40,13 +49,15 @@ cudaError_t launch_one_pair(const CUtensorMap& ta, const CUtensorMap& tb, const 
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // the kernel waits (griddepcontrol.wait)
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, kern, ta, tb, a);
 }
 
