@@ -47,21 +47,7 @@ struct LayoutPair {
 
 template <int BN>
 __device__ __forceinline__ Unit decode_unit_pair(const Args& a, long long u) {
-  Unit r;
-  r.split = int(u % a.splits);
-  const long long tile = u / a.splits;
-  const long long per_batch = (long long)a.tiles_m * a.tiles_n;
-  r.b = int(tile / per_batch);
-  const int t = int(tile % per_batch);
-  const int span = a.group_m * a.tiles_n;
-  const int first_m = (t / span) * a.group_m;
-  const int gsize = min(a.tiles_m - first_m, a.group_m);
-  const int rr = t % span;
-  r.m0 = (first_m + rr % gsize) * BM_PAIR;
-  r.n0 = (rr / gsize) * BN;
-  r.kb0 = r.split * a.kb_per_split;
-  r.nkb = min(a.kb_total - r.kb0, a.kb_per_split);
-  return r;
+  return decode_unit_tm<BM_PAIR, BN>(a, u);
 }
 
 template <class T, int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
@@ -249,14 +235,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::tc_fence_after();
       const int row = u.m0 + row_in_tile;
       const uint32_t t_row = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN);
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        ptx::tmem_ld_32x32b_x32(t_row + uint32_t(c * 32), r);
-        ptx::tmem_ld_wait(r);
-        const int col = u.n0 + c * 32;
-        if (row < a.M && col < a.N) epilogue_chunk<T, EPI>(a, u, row, col, r);
-      }
+      drain_rows<T, EPI, BN>(a, u, row, t_row);
       ptx::tc_fence_before();
       ptx::mbar_arrive_cluster(ptx::map_to_rank(tempty_bar(acc), 0));  // this half of the accumulator is free
       acc ^= 1;

@@ -87,30 +87,53 @@ struct Layout {
   static constexpr int ALLOC = BYTES + 1024;  // dynamic smem requested (1024-byte alignment slack)
   static constexpr int TMEM_COLS = 2 * BN;
   static_assert(A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "tiles must stay 1024-byte aligned");
-  static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation is a power of two");
+  static_assert(TMEM_COLS >= 32 && TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0,
+                "TMEM allocation is a power of two of at least 32 columns");
 };
 
 struct Unit {
   int b, m0, n0, split, kb0, nkb;
 };
 
-template <int BN>
-__device__ __forceinline__ Unit decode_unit(const Args& a, long long u) {
+// Unit -> (split, batch, tile) in the grouped raster, for TM-row tiles. Units
+// stay below 2^29 (the host refuses larger plans), so 32-bit unsigned
+// arithmetic is exact; the split and batch divisions are skipped when there is
+// one of them (a 64-bit division by a run-time value is a long emulated
+// sequence, measured at ~0.7 us before a small GEMM's first load).
+template <int TM, int BN>
+__device__ __forceinline__ Unit decode_unit_tm(const Args& a, long long unit) {
+  const unsigned u = unsigned(unit);
   Unit r;
-  r.split = int(u % a.splits);
-  const long long tile = u / a.splits;
-  const long long per_batch = (long long)a.tiles_m * a.tiles_n;
-  r.b = int(tile / per_batch);
-  const int t = int(tile % per_batch);
-  const int span = a.group_m * a.tiles_n;
-  const int first_m = (t / span) * a.group_m;
-  const int gsize = min(a.tiles_m - first_m, a.group_m);
-  const int rr = t % span;
-  r.m0 = (first_m + rr % gsize) * BM;
-  r.n0 = (rr / gsize) * BN;
+  unsigned tile = u;
+  r.split = 0;
+  if (a.splits > 1) {
+    tile = u / unsigned(a.splits);
+    r.split = int(u - tile * unsigned(a.splits));
+  }
+  unsigned t = tile;
+  r.b = 0;
+  if (a.batch > 1) {
+    const unsigned per_batch = unsigned(a.tiles_m) * unsigned(a.tiles_n);
+    const unsigned b = tile / per_batch;
+    r.b = int(b);
+    t = tile - b * per_batch;
+  }
+  const unsigned span = unsigned(a.group_m) * unsigned(a.tiles_n);
+  const unsigned grp = t / span;
+  const unsigned first_m = grp * unsigned(a.group_m);
+  const unsigned gsize = min(unsigned(a.tiles_m) - first_m, unsigned(a.group_m));
+  const unsigned rr = t - grp * span;
+  const unsigned ni = rr / gsize;
+  r.m0 = int((first_m + (rr - ni * gsize)) * unsigned(TM));
+  r.n0 = int(ni * unsigned(BN));
   r.kb0 = r.split * a.kb_per_split;
   r.nkb = min(a.kb_total - r.kb0, a.kb_per_split);
   return r;
+}
+
+template <int BN>
+__device__ __forceinline__ Unit decode_unit(const Args& a, long long u) {
+  return decode_unit_tm<BM, BN>(a, u);
 }
 
 // ------------------------------------------------------------- epilogue
@@ -171,6 +194,30 @@ __device__ __forceinline__ void epilogue_chunk(const Args& a, const Unit& u, int
       T* dst = static_cast<T*>(a.peers[p]) + (long long)row * a.ldc + a.col_offset + col;
       store_row_chunk<T>(dst, v, ncols);
     }
+  }
+}
+
+// Reads this warp's 32 rows of a BN-column accumulator from TMEM and hands
+// each 32-column chunk to the epilogue. Two register buffers: the next
+// chunk's TMEM load is in flight while the current one is converted and
+// stored, so a tile costs about one load latency instead of BN/32 of them
+// (tcgen05.wait::ld waits for every load this thread has issued, and only
+// one is outstanding at each wait). ld and wait run on the whole warp.
+template <class T, int EPI, int BN>
+__device__ __forceinline__ void drain_rows(const Args& a, const Unit& u, int row, uint32_t t_row) {
+  static_assert(BN % 64 == 0, "chunks are taken in pairs");
+  uint32_t r0[32], r1[32];
+  ptx::tmem_ld_32x32b_x32(t_row, r0);
+#pragma unroll 1
+  for (int c = 0; c < BN / 32; c += 2) {
+    ptx::tmem_ld_wait(r0);
+    ptx::tmem_ld_32x32b_x32(t_row + uint32_t((c + 1) * 32), r1);
+    const int col0 = u.n0 + c * 32;
+    if (row < a.M && col0 < a.N) epilogue_chunk<T, EPI>(a, u, row, col0, r0);
+    ptx::tmem_ld_wait(r1);
+    if (c + 2 < BN / 32) ptx::tmem_ld_32x32b_x32(t_row + uint32_t((c + 2) * 32), r0);
+    const int col1 = col0 + 32;
+    if (row < a.M && col1 < a.N) epilogue_chunk<T, EPI>(a, u, row, col1, r1);
   }
 }
 
@@ -353,14 +400,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::tc_fence_after();
       const int row = u.m0 + row_in_tile;
       const uint32_t t_row = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN);
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        ptx::tmem_ld_32x32b_x32(t_row + uint32_t(c * 32), r);
-        ptx::tmem_ld_wait(r);
-        const int col = u.n0 + c * 32;
-        if (row < a.M && col < a.N) epilogue_chunk<T, EPI>(a, u, row, col, r);
-      }
+      drain_rows<T, EPI, BN>(a, u, row, t_row);
       ptx::tc_fence_before();
       ptx::mbar_arrive(tempty_bar(acc));
       acc ^= 1;

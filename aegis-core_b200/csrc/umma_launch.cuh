@@ -99,8 +99,8 @@ cudaError_t launch_epi(const LaunchKey& k, const CUtensorMap& ta, const CUtensor
   }
 }
 
-// The instantiations the registry lists (gemm::UMMA_CONFIGS): one CTA (256, 4)
-// and (128, 6); CTA pairs (256, gemm::kUmmaPairStages).
+// The instantiations the registry lists (gemm::UMMA_CONFIGS): one CTA (256, 4),
+// (128, 6) and (64, 8); CTA pairs (256, gemm::kUmmaPairStages).
 template <class T>
 cudaError_t launch_family(const LaunchKey& k, const CUtensorMap& ta, const CUtensorMap& tb, const Args& a,
                           int grid, cudaStream_t s) {
@@ -111,6 +111,7 @@ cudaError_t launch_family(const LaunchKey& k, const CUtensorMap& ta, const CUten
   }
   if (k.BN == 256 && k.STAGES == 4) return launch_epi<T, 256, 4, false>(k, ta, tb, a, grid, s);
   if (k.BN == 128 && k.STAGES == 6) return launch_epi<T, 128, 6, false>(k, ta, tb, a, grid, s);
+  if (k.BN == 64 && k.STAGES == 8) return launch_epi<T, 64, 8, false>(k, ta, tb, a, grid, s);
   return cudaErrorNotSupported;
 }
 
@@ -124,6 +125,7 @@ cudaError_t attrs_family(int BN, int STAGES, bool pair, cudaFuncAttributes* attr
   }
   if (BN == 256 && STAGES == 4) return attrs_one<T, 256, 4, false, true, kEpiStore>(attrs);
   if (BN == 128 && STAGES == 6) return attrs_one<T, 128, 6, false, true, kEpiStore>(attrs);
+  if (BN == 64 && STAGES == 8) return attrs_one<T, 64, 8, false, true, kEpiStore>(attrs);
   return cudaErrorNotSupported;
 }
 

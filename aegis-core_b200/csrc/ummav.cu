@@ -45,7 +45,7 @@ constexpr int kThreads = 192;
 struct Args {
   int M, N, K;
   int tiles, kb;        // column tiles, k-blocks per tile
-  long long total;      // tiles * kb
+  unsigned total;       // tiles * kb (the host keeps total * grid below 2^32)
   void* C;
   long long ldc;
   float alpha, beta;
@@ -72,13 +72,16 @@ struct Layout {
   static_assert(A_OFF % 1024 == 0 && BAR_OFF % 8 == 0, "operand tiles stay 1024-byte aligned");
 };
 
-__device__ __forceinline__ long long range_start(const Args& a, long long c) {
+// 32-bit arithmetic throughout: total * gridDim.x < 2^32 (host check), and a
+// 64-bit division by a run-time value is a long emulated sequence on the
+// critical path of a microsecond-scale kernel.
+__device__ __forceinline__ unsigned range_start(const Args& a, unsigned c) {
   return a.total * c / gridDim.x;
 }
 
 // The CTA whose range holds linear k-block x.
-__device__ __forceinline__ int owner_of(const Args& a, long long x) {
-  long long c = x * gridDim.x / a.total;
+__device__ __forceinline__ int owner_of(const Args& a, unsigned x) {
+  unsigned c = x * gridDim.x / a.total;
   while (c + 1 < gridDim.x && range_start(a, c + 1) <= x) ++c;
   while (c > 0 && range_start(a, c) > x) --c;
   return int(c);
@@ -140,12 +143,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   // grids this one depends on have completed.
   ptx::griddep_wait();
 
-  const long long r0 = range_start(a, blockIdx.x), r1 = range_start(a, blockIdx.x + 1);
-  auto next_seg = [&](long long pos) {
+  const unsigned r0 = range_start(a, blockIdx.x), r1 = range_start(a, blockIdx.x + 1);
+  auto next_seg = [&](unsigned pos) {
     Seg s;
-    s.tile = int(pos / a.kb);
-    s.kb0 = int(pos % a.kb);
-    s.nkb = int(min((long long)(a.kb - s.kb0), r1 - pos));
+    const unsigned t = pos / unsigned(a.kb);
+    s.tile = int(t);
+    s.kb0 = int(pos - t * unsigned(a.kb));
+    s.nkb = int(min(unsigned(a.kb - s.kb0), r1 - pos));
     return s;
   };
 
@@ -157,7 +161,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (long long pos = r0; pos < r1 && ok;) {
+      for (unsigned pos = r0; pos < r1 && ok;) {
         const Seg sg = next_seg(pos);
         for (int i = 0; i < sg.nkb; ++i) {
           ok = ptx::mbar_wait_bounded(empty_bar(stage), phase ^ 1u, abort_flag, a.status, kStatusTimeoutProducer,
@@ -195,7 +199,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0, acc = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
-      for (long long pos = r0; pos < r1 && ok;) {
+      for (unsigned pos = r0; pos < r1 && ok;) {
         const Seg sg = next_seg(pos);
         ok = ptx::mbar_wait_bounded(tempty_bar(acc), acc_phase ^ 1u, abort_flag, a.status, kStatusTimeoutMma,
                                     a.wait_limit_ns);
@@ -237,7 +241,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
-    for (long long pos = r0; pos < r1 && ok;) {
+    for (unsigned pos = r0; pos < r1 && ok;) {
       const Seg sg = next_seg(pos);
       if (lane == 0)
         ok = ptx::mbar_wait_bounded(tfull_bar(acc), acc_phase, abort_flag, a.status, kStatusTimeoutEpilogue,
@@ -253,7 +257,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
 
-      const long long tile_first = (long long)sg.tile * a.kb;
+      const unsigned tile_first = unsigned(sg.tile) * unsigned(a.kb);
       const int c_first = owner_of(a, tile_first);
       const int nseg = owner_of(a, tile_first + a.kb - 1) - c_first + 1;
       const int n = sg.tile * BMN + row;
@@ -402,6 +406,10 @@ cudaError_t ummav_run(int cfg, const gemm::GemmParams& p, cudaStream_t stream) {
   if (p.alpha == 0.f) return scale_c(p, stream);
   if (!ummav_applicable(p)) return gemv_run(p.M <= 4 ? 0 : (p.M <= 8 ? 1 : 2), p, stream);
   const ummav::Plan pl = ummav::make_plan(cfg, p);
+  // The kernel's position arithmetic is 32-bit: total * grid < 2^32 (about
+  // 2e11 weight elements at 296 CTAs, far beyond device memory).
+  if ((unsigned long long)pl.total * (unsigned long long)pl.grid >= (1ull << 32))
+    return gemv_run(p.M <= 4 ? 0 : (p.M <= 8 ? 1 : 2), p, stream);
   CUtensorMap ta, tb;
   if (!encode_map(&ta, p.dtype, p.A, p.K, p.M, p.lda, 1, 0, ummav::MPAD) ||
       !encode_map(&tb, p.dtype, p.B, p.N, p.K, p.ldb, 1, 0, ummav::BK))
@@ -412,7 +420,7 @@ cudaError_t ummav_run(int cfg, const gemm::GemmParams& p, cudaStream_t stream) {
   a.K = p.K;
   a.tiles = pl.tiles;
   a.kb = pl.kb;
-  a.total = pl.total;
+  a.total = unsigned(pl.total);
   a.C = p.C;
   a.ldc = p.ldc;
   a.alpha = p.alpha;

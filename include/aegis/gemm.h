@@ -130,6 +130,10 @@ inline constexpr UmmaConfig UMMA_CONFIGS[] = {
     {128, 128, 64, 6, 1, 1},
     {256, 256, 64, kUmmaPairStages, 0, 2},
     {256, 256, 64, kUmmaPairStages, 1, 2},
+    // Small problems: 128 x 64 tiles, an 8-deep ring of 24 KB stages (twice
+    // the CTAs of 128 x 128 tiles, and K = 512 fully in flight).
+    {128, 64, 64, 8, 0, 1},
+    {128, 64, 64, 8, 1, 1},
 };
 std::span<const KernelEntry> umma_entries();
 
