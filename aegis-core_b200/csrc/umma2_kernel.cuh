@@ -240,6 +240,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mbar_arrive_cluster(ptx::map_to_rank(tempty_bar(acc), 0));  // this half of the accumulator is free
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
+      if constexpr (EPI == kEpiPeers) push_warp_rows<T, BN>(a, u, u.m0 + 128 * int(rank) + quarter * 32, lane);
       long long next = -1;
       if (lane == 0) ok = sched_take(sched, seq, rank != 0, &next, kStatusTimeoutEpilogue);
       ok = __shfl_sync(0xffffffffu, ok, 0);

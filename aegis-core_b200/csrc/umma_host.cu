@@ -283,8 +283,6 @@ cudaError_t launch(const GemmParams& p, const umma::LaunchKey& k, const Maps& m,
 // split-K (measured equal to or faster than one-CTA 128 x 256 tiles at
 // 4096^3 .. 16384^3).
 constexpr int kNshardConfig = 4;
-// Ranks up to which the all-gather stays fused in the GEMM epilogue.
-constexpr int kFusedGatherMaxRanks = 2;
 static_assert(gemm::UMMA_CONFIGS[kNshardConfig].CTAS == 2 && gemm::UMMA_CONFIGS[kNshardConfig].BN == 256 &&
                   !gemm::UMMA_CONFIGS[kNshardConfig].SPLITK,
               "the N-sharded path needs the non-split CTA-pair config");
@@ -343,62 +341,6 @@ size_t umma_smem_bytes(int cfg) {
   return c.BN == 256 ? size_t(umma::Layout<256, 4>::ALLOC) : size_t(umma::Layout<128, 6>::ALLOC);
 }
 
-namespace {
-
-struct PeerList {
-  uint16_t* p[umma::kMaxPeers];
-};
-
-// The all-gather half of the N-sharded GEMM for 3 or more ranks: copies this
-// rank's finished column shard (M rows x ns columns of the 16-bit C at
-// col_offset) into the same place of every peer's C. Consecutive lanes take
-// consecutive 16-byte pieces of a row, so every warp store writes 512
-// contiguous bytes over NVLink (the epilogue's row-per-thread stores reach a
-// fraction of the link bandwidth once several peers share them). U pieces per
-// thread are loaded before any store. `vec`: 16-byte pieces (aligned bases,
-// ldc, col_offset and ns multiples of 8), else single elements.
-template <int U>
-__global__ void __launch_bounds__(256) push_shard_kernel(const uint16_t* __restrict__ src, long long ldc,
-                                                         int col_offset, int ns, int M, PeerList dst, int ndst,
-                                                         int vec) {
-  const int w = vec ? 8 : 1;
-  const long long per_row = ns / w;
-  const long long total = (long long)M * per_row;
-  const long long stride = (long long)gridDim.x * blockDim.x;
-  for (long long t0 = blockIdx.x * (long long)blockDim.x + threadIdx.x; t0 < total; t0 += stride * U) {
-    if (vec) {
-      uint4 v[U];
-      long long off[U];
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const long long t = t0 + u * stride;
-        off[u] = -1;
-        if (t < total) {
-          const long long r = t / per_row, c = t - r * per_row;
-          off[u] = r * ldc + col_offset + c * 8;
-          v[u] = __ldg(reinterpret_cast<const uint4*>(src + off[u]));
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < U; ++u)
-        if (off[u] >= 0)
-          for (int q = 0; q < ndst; ++q) *reinterpret_cast<uint4*>(dst.p[q] + off[u]) = v[u];
-    } else {
-      for (int u = 0; u < U; ++u) {
-        const long long t = t0 + u * stride;
-        if (t >= total) break;
-        const long long r = t / per_row, c = t - r * per_row;
-        const long long o = r * ldc + col_offset + c;
-        const uint16_t x = src[o];
-        for (int q = 0; q < ndst; ++q) dst.p[q][o] = x;
-      }
-    }
-  }
-  __threadfence_system();  // the peer stores are complete before the kernel ends
-}
-
-}  // namespace
-
 cudaError_t umma_nsharded(const GemmParams& local, void* const* c_ranks, int nranks, int col_offset,
                           cudaStream_t stream) {
   if (nranks < 1 || nranks > umma::kMaxPeers || !c_ranks) return cudaErrorInvalidValue;
@@ -414,33 +356,22 @@ cudaError_t umma_nsharded(const GemmParams& local, void* const* c_ranks, int nra
   a.col_offset = col_offset;
   for (int i = 0; i < nranks; ++i)
     if (!c_ranks[i]) return cudaErrorInvalidValue;
-  // Up to 2 ranks the epilogue stores each finished tile straight into every
-  // rank's C (measured equal to a GEMM + NCCL all-gather at 2 GPUs). From 3
-  // ranks on, its row-per-thread peer stores throttle the GEMM: the epilogue
-  // then stores locally and push_shard_kernel copies the shard to the peers
-  // with coalesced stores, in stream order.
-  const bool fused = nranks <= kFusedGatherMaxRanks;
-  if (fused) {
-    a.npeers = nranks;
-    for (int i = 0; i < nranks; ++i) a.peers[i] = c_ranks[i];
-  } else {
-    a.npeers = 1;
-    a.peers[0] = local.C;
-  }
-  const umma::LaunchKey k{pl.BN, pl.STAGES, false, true, umma::kEpiPeers, pl.CTAS == 2};
-  if (const cudaError_t e = launch(local, k, maps, a, pl.grid, stream); e != cudaSuccess || fused) return e;
-  PeerList dst{};
-  int ndst = 0;
+  // The epilogue stores each finished tile into this rank's C, then each warp
+  // copies its rows to the other ranks with row-contiguous stores
+  // (push_warp_rows), overlapping the next tile's main loop.
+  a.peers[0] = local.C;
+  int np = 1;
   for (int i = 0; i < nranks; ++i)
-    if (c_ranks[i] != local.C) dst.p[ndst++] = static_cast<uint16_t*>(c_ranks[i]);
-  bool vec = local.ldc % 8 == 0 && col_offset % 8 == 0 && local.N % 8 == 0 &&
-             (reinterpret_cast<uintptr_t>(local.C) & 15u) == 0;
-  for (int i = 0; i < ndst; ++i) vec = vec && (reinterpret_cast<uintptr_t>(dst.p[i]) & 15u) == 0;
-  const hw::DeviceLimits* d = hw::physical();
-  const int blocks = (d ? d->sm_count : 148) * 4;
-  push_shard_kernel<4><<<blocks, 256, 0, stream>>>(static_cast<const uint16_t*>(local.C), local.ldc, col_offset,
-                                                   local.N, local.M, dst, ndst, vec ? 1 : 0);
-  return cudaGetLastError();
+    if (c_ranks[i] != local.C) {
+      if (np >= nranks) return cudaErrorInvalidValue;  // local.C must be one of c_ranks
+      a.peers[np++] = c_ranks[i];
+    }
+  a.npeers = np;  // entries equal to local.C are this rank's own C
+  bool vec = local.ldc % 8 == 0 && col_offset % 8 == 0;
+  for (int i = 0; i < np; ++i) vec = vec && (reinterpret_cast<uintptr_t>(a.peers[i]) & 15u) == 0;
+  a.peer_vec = vec ? 1 : 0;
+  const umma::LaunchKey k{pl.BN, pl.STAGES, false, true, umma::kEpiPeers, pl.CTAS == 2};
+  return launch(local, k, maps, a, pl.grid, stream);
 }
 
 }  // namespace aegis

@@ -66,8 +66,9 @@ struct Args {
   long long ldc, stride_c;
   float alpha, beta;
   float* partials;           // kEpiPartial: [split][batch][M][N] FP32
-  void* peers[kMaxPeers];    // kEpiPeers: every rank's C (row-major, ldc)
+  void* peers[kMaxPeers];    // kEpiPeers: this rank's C first, then every other rank's (row-major, ldc)
   int npeers, col_offset;    // kEpiPeers: ranks; this rank's first column
+  int peer_vec;              // kEpiPeers: 16-byte pushes (aligned bases, ldc and col_offset % 8 == 0)
   unsigned* status;          // per-device watchdog word
   long long wait_limit_ns;
 };
@@ -187,12 +188,56 @@ __device__ __forceinline__ void epilogue_chunk(const Args& a, const Unit& u, int
         if (i < ncols) v[i] += a.beta * E::to_f32(dst[i]);
     }
     store_row_chunk<T>(dst, v, ncols);
-  } else {  // kEpiPeers: plain C = A*B, the same tile into every rank's C
+  } else {  // kEpiPeers: plain C = A*B into this rank's C (push_warp_rows copies it to the peers)
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-    for (int p = 0; p < a.npeers; ++p) {
-      T* dst = static_cast<T*>(a.peers[p]) + (long long)row * a.ldc + a.col_offset + col;
-      store_row_chunk<T>(dst, v, ncols);
+    T* dst = static_cast<T*>(a.peers[0]) + (long long)row * a.ldc + a.col_offset + col;
+    store_row_chunk<T>(dst, v, ncols);
+  }
+}
+
+// kEpiPeers, after the warp has stored its 32 rows of the tile into this
+// rank's C and released the accumulator: copies those rows into every other
+// rank's C over NVLink. The rows are read back (L2) with the lanes across the
+// columns, so each warp store writes 512 contiguous bytes of one row; stored
+// straight from the TMEM layout (one row per lane) they were 16-byte pieces of
+// 32 rows per instruction, a fraction of the link bandwidth once several
+// peers share them. Eight rows' loads are in flight before their stores. The
+// copy overlaps the main loop of the next tile (the epilogue warps are
+// otherwise idle there).
+template <class T, int BN>
+__device__ __forceinline__ void push_warp_rows(const Args& a, const Unit& u, int row_first, int lane) {
+  static_assert(BN == 256, "one 16-byte piece per lane per row");
+  __syncwarp();  // the warp's own stores are visible to all its lanes
+  if (a.npeers < 2) return;
+  const int ncols = min(BN, a.N - u.n0);
+  const T* src = static_cast<const T*>(a.peers[0]);
+  const bool vec = a.peer_vec && ncols == BN;
+#pragma unroll 1
+  for (int i0 = 0; i0 < 32; i0 += 8) {
+    if (vec) {
+      uint4 v[8];
+      long long off[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int r = row_first + i0 + i;
+        off[i] = r < a.M ? (long long)r * a.ldc + a.col_offset + u.n0 + lane * 8 : -1;
+        if (off[i] >= 0) v[i] = __ldcg(reinterpret_cast<const uint4*>(src + off[i]));
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (off[i] >= 0)
+          for (int p = 1; p < a.npeers; ++p) *reinterpret_cast<uint4*>(static_cast<T*>(a.peers[p]) + off[i]) = v[i];
+    } else {
+      for (int i = 0; i < 8; ++i) {
+        const int r = row_first + i0 + i;
+        if (r >= a.M) break;
+        const long long base = (long long)r * a.ldc + a.col_offset + u.n0;
+        for (int c = lane; c < ncols; c += 32) {
+          const T x = src[base + c];
+          for (int p = 1; p < a.npeers; ++p) static_cast<T*>(a.peers[p])[base + c] = x;
+        }
+      }
     }
   }
 }
@@ -405,6 +450,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mbar_arrive(tempty_bar(acc));
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
+      if constexpr (EPI == kEpiPeers) push_warp_rows<T, BN>(a, u, u.m0 + quarter * 32, lane);
       long long next = -1;
       if (lane == 0) ok = sched_take(sched, seq, false, &next, kStatusTimeoutEpilogue);
       ok = __shfl_sync(0xffffffffu, ok, 0);
