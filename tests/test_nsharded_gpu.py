@@ -52,3 +52,33 @@ def test_argument_checks(cuda):
         ctx.nsharded(16, 32, 16, p, 16, p, 8, [p, p], 16, 2, 0)          # ldc < N
     with pytest.raises(ac.AegisError):
         ctx.nsharded(16, 32, 16, p, 16, p, 8, [p, p], 32, 2, 2)          # rank out of range
+
+
+@pytest.mark.parametrize("nranks", [2, 4])
+def test_emulated_ranks_ragged_tiles_and_padded_ldc(cuda, nranks):
+    """Partial tiles in M and in the shard's columns (ns = 208 at 4 ranks, 416 at
+    2) and an odd padded ldc: the peer copy takes its element-wise path, and
+    C's padding columns stay untouched."""
+    torch = cuda
+    M, N, K, pad = 300, 832, 264, 3
+    ldc = N + pad
+    g = ac.Generator(77)
+    A, B = g.uniform(M * K, "bf16"), g.uniform(K * N, "bf16")
+    ctx = context(torch)
+    dA, dB = dev(torch, A), dev(torch, B)
+    full = dev(torch, np.zeros(M * N, np.uint16))
+    ctx.gemm(dA.data_ptr(), dB.data_ptr(), full.data_ptr(), M, N, K, ac.DTYPE_BF16)
+    ctx.synchronize()
+    want = host(full).reshape(M, N)
+    ns = N // nranks
+    Bm = B.reshape(K, N)
+    shards = [dev(torch, np.ascontiguousarray(Bm[:, r * ns:(r + 1) * ns])) for r in range(nranks)]
+    cs = [dev(torch, np.full(M * ldc, 0x7FC0, np.uint16)) for _ in range(nranks)]
+    for r in range(nranks):
+        ctx.nsharded(M, N, K, dA.data_ptr(), K, shards[r].data_ptr(), ns, [c.data_ptr() for c in cs], ldc, nranks,
+                     r, ac.DTYPE_BF16)
+    ctx.synchronize()
+    for r in range(nranks):
+        got = host(cs[r]).reshape(M, ldc)
+        assert np.array_equal(got[:, :N], want), f"rank {r} of {nranks}"
+        assert (got[:, N:] == 0x7FC0).all(), "padding columns written"
