@@ -55,4 +55,51 @@ enum StatusBits : unsigned {
 // contexts on a shared GPU.
 inline constexpr long long kDefaultWaitLimitNs = 2000000000ll;
 
+// Split-K slot sums: p[0] + p[stride] + ... + p[(S-1)*stride] in that fixed
+// order (the first slot taken as is, each next one added, exactly as a plain
+// sequential loop does), with the L2 loads issued eight at a time so S slots
+// cost about S/8 round trips instead of S.
+__device__ __forceinline__ float sum_slots(const float* p, long long stride, int S) {
+  float acc = 0.f;
+  int q = 0;
+  for (; q + 8 <= S; q += 8) {
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = __ldcg(p + (long long)(q + j) * stride);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc = (q + j == 0) ? v[j] : acc + v[j];
+  }
+  for (; q < S; ++q) {
+    const float v = __ldcg(p + (long long)q * stride);
+    acc = (q == 0) ? v : acc + v;
+  }
+  return acc;
+}
+__device__ __forceinline__ float4 sum_slots4(const float4* p, long long stride, int S) {
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  int q = 0;
+  for (; q + 8 <= S; q += 8) {
+    float4 v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = __ldcg(p + (long long)(q + j) * stride);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (q + j == 0) {
+        acc = v[j];
+      } else {
+        acc.x += v[j].x; acc.y += v[j].y; acc.z += v[j].z; acc.w += v[j].w;
+      }
+    }
+  }
+  for (; q < S; ++q) {
+    const float4 v = __ldcg(p + (long long)q * stride);
+    if (q == 0) {
+      acc = v;
+    } else {
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+  }
+  return acc;
+}
+
 }  // namespace aegis

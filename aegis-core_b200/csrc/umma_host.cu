@@ -96,11 +96,7 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
     const long long off = bm * N + n;
     T* c = C + b * stride_c + (long long)m * ldc + n;
     if constexpr (VEC4) {
-      float4 acc = __ldcg(reinterpret_cast<const float4*>(part + off));
-      for (int s = 1; s < S; ++s) {
-        const float4 q = __ldcg(reinterpret_cast<const float4*>(part + s * plane + off));
-        acc.x += q.x; acc.y += q.y; acc.z += q.z; acc.w += q.w;
-      }
+      const float4 acc = sum_slots4(reinterpret_cast<const float4*>(part + off), plane / 4, S);  // in split order
       float v[4] = {alpha * acc.x, alpha * acc.y, alpha * acc.z, alpha * acc.w};
       if (beta != 0.f)
         for (int j = 0; j < 4; ++j) v[j] += beta * E::to_f32(c[j]);
@@ -113,8 +109,7 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
         for (int j = 0; j < 4; ++j) c[j] = E::from_f32(v[j]);
       }
     } else {
-      float acc = __ldcg(part + off);
-      for (int s = 1; s < S; ++s) acc += __ldcg(part + s * plane + off);
+      const float acc = sum_slots(part + off, plane, S);  // in split order
       float v = alpha * acc;
       if (beta != 0.f) v += beta * E::to_f32(*c);
       *c = E::from_f32(v);
