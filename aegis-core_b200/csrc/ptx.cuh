@@ -249,34 +249,9 @@ __device__ __forceinline__ uint32_t map_to_rank(uint32_t local_addr, uint32_t ra
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_addr), "r"(rank));
   return r;
 }
-__device__ __forceinline__ uint32_t cluster_nctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ uint32_t cluster_id_x() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
-  return r;
-}
 // Every thread of every CTA of the cluster (aligned: whole warps).
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-// The two halves of cluster_sync, for work between them: every thread
-// arrives once, then waits once before it arrives again.
-__device__ __forceinline__ void cluster_arrive() {
-  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void cluster_wait() {
-  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-// 16-byte store to another CTA's shared memory (cluster address).
-__device__ __forceinline__ void st_cluster_v4(uint32_t cluster_addr, uint32_t x, uint32_t y, uint32_t z,
-                                              uint32_t w) {
-  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr), "r"(x), "r"(y), "r"(z),
-               "r"(w)
-               : "memory");
 }
 // Arrive on an mbarrier in another CTA of the cluster (release at cluster scope).
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {

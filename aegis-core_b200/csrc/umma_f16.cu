@@ -5,7 +5,4 @@ namespace aegis::umma {
 template cudaError_t launch_family<__half>(const LaunchKey&, const CUtensorMap&, const CUtensorMap&, const Args&,
                                            int, cudaStream_t);
 template cudaError_t attrs_family<__half>(int, int, bool, cudaFuncAttributes*);
-template cudaError_t launch_cluster_family<__half>(const LaunchKey&, const CUtensorMap&,
-                                                         const CUtensorMap&, const Args&, int, int, cudaStream_t);
-template cudaError_t attrs_cluster_family<__half>(int, int, cudaFuncAttributes*);
 }  // namespace aegis::umma

@@ -151,7 +151,6 @@ struct Plan {
   int tiles_m = 0, tiles_n = 0;
   int group_m = umma::kGroupM;
   bool steal = true;  // more units than resident CTAs (pairs)
-  bool cluster = false;  // cluster split-K (SPLITK == 2): `splits` CTAs per cluster, one tile each
   long long tiles = 0, units = 0;
   int grid = 0;
 };
@@ -220,20 +219,7 @@ Plan make_plan(int cfg, const GemmParams& p) {
   // Tile slots: one per SM, or one per resident pair of SMs for cta_group::2.
   const int sms = d ? (c.CTAS == 2 ? pair_slots(d->sm_count / 2) : d->sm_count) : 0;
   int S = 1;
-  if (c.SPLITK == 2) {
-    // Cluster split-K: the largest S in {1, 2, 4, 8} with tiles * S CTAs
-    // within the SM count and at least one k-block per CTA.
-    if (sms > 0)
-      while (2 * S <= umma::kMaxClusterSplits && pl.tiles * 2 * S <= sms && 2 * S <= pl.kb_total) S *= 2;
-    pl.cluster = true;
-    pl.splits = S;
-    pl.kb_per_split = ceil_div(pl.kb_total, S);
-    pl.units = pl.tiles;
-    pl.grid = int(std::max<long long>(1, std::min<long long>(pl.units, kMaxUnits))) * S;
-    pl.steal = false;
-    return pl;
-  }
-  if (c.SPLITK == 1 && sms > 0 && pl.tiles < sms) {
+  if (c.SPLITK && sms > 0 && pl.tiles < sms) {
     // One k-block is BK/16 = 4 MMAs of 128 x BN x 16 (about 128 cycles each at
     // BN = 256 on one SM, ~1.85 GHz). The reduction moves 8 bytes per output
     // element per split (write + read FP32) at ~5 TB/s.
@@ -288,12 +274,6 @@ cudaError_t launch(const GemmParams& p, const umma::LaunchKey& k, const Maps& m,
                                 : umma::launch_family<__half>(k, m.a, m.b, a, grid, s);
 }
 
-cudaError_t launch_cluster(const GemmParams& p, const umma::LaunchKey& k, const Maps& m, const umma::Args& a,
-                           int splits, int grid, cudaStream_t s) {
-  return p.dtype == DType::BF16 ? umma::launch_cluster_family<__nv_bfloat16>(k, m.a, m.b, a, splits, grid, s)
-                                : umma::launch_cluster_family<__half>(k, m.a, m.b, a, splits, grid, s);
-}
-
 // The N-sharded GEMM runs UMMA_CONFIGS[4]: CTA pairs, 256 x 256 tiles, no
 // split-K (measured equal to or faster than one-CTA 128 x 256 tiles at
 // 4096^3 .. 16384^3).
@@ -322,16 +302,6 @@ cudaError_t umma_run(int cfg, const GemmParams& p, cudaStream_t stream) {
   if (const cudaError_t e = status::word(&a.status); e != cudaSuccess) return e;
   umma::LaunchKey k{pl.BN, pl.STAGES, p.layout_a == Layout::ColMajor, p.layout_b == Layout::RowMajor,
                     umma::kEpiStore, pl.CTAS == 2};
-  if (pl.cluster) {
-    // One tile per cluster: the kernel walks tiles only and slices K by its
-    // cluster rank.
-    a.splits = 1;
-    a.kb_per_split = pl.kb_total;
-    a.units = pl.tiles;
-    a.c_vec4 = (reinterpret_cast<uintptr_t>(p.C) & 7u) == 0 && p.ldc % 4 == 0 &&
-               (p.batch <= 1 || p.stride_c % 4 == 0);
-    return launch_cluster(p, k, maps, a, pl.splits, pl.grid, stream);
-  }
   if (pl.splits == 1) return launch(p, k, maps, a, pl.grid, stream);
   // Split-K: partials, then the ordered reduction.
   void* part = nullptr;
@@ -356,15 +326,12 @@ gemm::LaunchPlan umma_plan(int cfg, const GemmParams& p) {
 
 cudaError_t umma_attrs(int cfg, cudaFuncAttributes* attrs) {
   const gemm::UmmaConfig& c = gemm::UMMA_CONFIGS[cfg];
-  if (c.SPLITK == 2) return umma::attrs_cluster_family<__half>(c.BN, c.STAGES, attrs);
   return umma::attrs_family<__half>(c.BN, c.STAGES, c.CTAS == 2, attrs);
 }
 
 size_t umma_smem_bytes(int cfg) {
   const gemm::UmmaConfig& c = gemm::UMMA_CONFIGS[cfg];
   if (c.CTAS == 2) return size_t(umma::LayoutPair<256, gemm::kUmmaPairStages>::ALLOC);
-  if (c.SPLITK == 2)
-    return c.BN == 64 ? size_t(umma::LayoutCluster<64, 6>::ALLOC) : size_t(umma::LayoutCluster<128, 4>::ALLOC);
   if (c.BN == 64) return size_t(umma::Layout<64, 8>::ALLOC);
   return c.BN == 256 ? size_t(umma::Layout<256, 4>::ALLOC) : size_t(umma::Layout<128, 6>::ALLOC);
 }

@@ -69,7 +69,6 @@ struct Args {
   void* peers[kMaxPeers];    // kEpiPeers: this rank's C first, then every other rank's (row-major, ldc)
   int npeers, col_offset;    // kEpiPeers: ranks; this rank's first column
   int peer_vec;              // kEpiPeers: 16-byte pushes (aligned bases, ldc and col_offset % 8 == 0)
-  int c_vec4;                // cluster split-K: 8-byte stores of 4 outputs (C, ldc, stride_c % 4 == 0)
   unsigned* status;          // per-device watchdog word
   long long wait_limit_ns;
 };

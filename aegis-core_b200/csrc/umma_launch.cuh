@@ -7,7 +7,6 @@
 #include "aegis/gemm.h"
 #include "device.h"
 #include "umma2_kernel.cuh"
-#include "umma_cluster_kernel.cuh"
 
 namespace aegis::umma {
 
@@ -130,64 +129,6 @@ cudaError_t attrs_family(int BN, int STAGES, bool pair, cudaFuncAttributes* attr
   return cudaErrorNotSupported;
 }
 
-// ---------------------------------------------------------------- cluster split-K (_kcl)
-template <class T, int BN, int STAGES, bool A_MN, bool B_MN>
-cudaError_t launch_one_cluster(const CUtensorMap& ta, const CUtensorMap& tb, const Args& a, int splits, int grid,
-                               cudaStream_t stream) {
-  auto* kern = &umma_cluster_kernel<T, BN, STAGES, A_MN, B_MN>;
-  static hw::PerDevice once;
-  constexpr size_t smem = size_t(LayoutCluster<BN, STAGES>::ALLOC);
-  if (const cudaError_t e = hw::configure_smem(once, kern, smem); e != cudaSuccess) return e;
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(unsigned(grid));
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = unsigned(splits);
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // the kernel waits (griddepcontrol.wait)
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, kern, ta, tb, a);
-}
-
-// The cluster split-K instantiations the registry lists: (64, 6) and (128, 4).
-// `splits`: the cluster size, 1, 2, 4 or 8; grid = tiles * splits.
-template <class T>
-cudaError_t launch_cluster_family(const LaunchKey& k, const CUtensorMap& ta, const CUtensorMap& tb, const Args& a,
-                                  int splits, int grid, cudaStream_t s) {
-  if (splits < 1 || splits > kMaxClusterSplits || (splits & (splits - 1)) != 0 || grid % splits != 0)
-    return cudaErrorInvalidValue;
-#define AEGIS_UMMA_CLUSTER(BNV, SV)                                                                            \
-  do {                                                                                                         \
-    if (!k.a_mn && k.b_mn) return launch_one_cluster<T, BNV, SV, false, true>(ta, tb, a, splits, grid, s);   \
-    if (!k.a_mn && !k.b_mn) return launch_one_cluster<T, BNV, SV, false, false>(ta, tb, a, splits, grid, s); \
-    if (k.a_mn && k.b_mn) return launch_one_cluster<T, BNV, SV, true, true>(ta, tb, a, splits, grid, s);     \
-    return launch_one_cluster<T, BNV, SV, true, false>(ta, tb, a, splits, grid, s);                          \
-  } while (0)
-  if (k.BN == 64 && k.STAGES == 6) AEGIS_UMMA_CLUSTER(64, 6);
-  if (k.BN == 128 && k.STAGES == 4) AEGIS_UMMA_CLUSTER(128, 4);
-#undef AEGIS_UMMA_CLUSTER
-  return cudaErrorNotSupported;
-}
-
-template <class T>
-cudaError_t attrs_cluster_family(int BN, int STAGES, cudaFuncAttributes* attrs) {
-  cudaError_t e = cudaErrorNotSupported;
-  if (BN == 64 && STAGES == 6) {
-    e = cudaFuncGetAttributes(attrs, &umma_cluster_kernel<T, 64, 6, false, true>);
-    if (e == cudaSuccess) attrs->sharedSizeBytes += LayoutCluster<64, 6>::ALLOC;
-  } else if (BN == 128 && STAGES == 4) {
-    e = cudaFuncGetAttributes(attrs, &umma_cluster_kernel<T, 128, 4, false, true>);
-    if (e == cudaSuccess) attrs->sharedSizeBytes += LayoutCluster<128, 4>::ALLOC;
-  }
-  return e;
-}
-
 // Explicit instantiations live in umma_f16.cu and umma_bf16.cu.
 extern template cudaError_t launch_family<__half>(const LaunchKey&, const CUtensorMap&, const CUtensorMap&,
                                                   const Args&, int, cudaStream_t);
@@ -195,12 +136,5 @@ extern template cudaError_t launch_family<__nv_bfloat16>(const LaunchKey&, const
                                                          const Args&, int, cudaStream_t);
 extern template cudaError_t attrs_family<__half>(int, int, bool, cudaFuncAttributes*);
 extern template cudaError_t attrs_family<__nv_bfloat16>(int, int, bool, cudaFuncAttributes*);
-extern template cudaError_t launch_cluster_family<__half>(const LaunchKey&, const CUtensorMap&, const CUtensorMap&,
-                                                          const Args&, int, int, cudaStream_t);
-extern template cudaError_t launch_cluster_family<__nv_bfloat16>(const LaunchKey&, const CUtensorMap&,
-                                                                 const CUtensorMap&, const Args&, int, int,
-                                                                 cudaStream_t);
-extern template cudaError_t attrs_cluster_family<__half>(int, int, cudaFuncAttributes*);
-extern template cudaError_t attrs_cluster_family<__nv_bfloat16>(int, int, cudaFuncAttributes*);
 
 }  // namespace aegis::umma

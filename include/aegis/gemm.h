@@ -117,12 +117,7 @@ const KernelEntry* find(std::string_view name);
 //           issues M = 256 MMAs into both CTAs' TMEM). No TMA multicast.
 // SPLITK: 0 = never split K; 1 = split K by the SM count when the tile count
 // alone cannot fill the GPU (partials reduced in a fixed order, bit-identical
-// across runs); 2 = split K over a thread-block cluster of S = 1, 2, 4 or 8
-// CTAs per tile (the most that keep tiles x S within the SM count), the
-// partial tiles reduced through distributed shared memory in slot order
-// 0..S-1 in the same launch (one tile per cluster, not persistent; for
-// problems of at most one wave). Name:
-// umma_<BM>x<BN>x<BK>_s<STAGES>[_c2][_ksm | _kcl].
+// across runs). Name: umma_<BM>x<BN>x<BK>_s<STAGES>[_c2][_ksm].
 // ---------------------------------------------------------------------------
 struct UmmaConfig { int BM, BN, BK, STAGES, SPLITK, CTAS; };
 // Ring depth of the CTA-pair configs: 7 x 32 KB stages fill the 227 KB of
@@ -139,9 +134,6 @@ inline constexpr UmmaConfig UMMA_CONFIGS[] = {
     // the CTAs of 128 x 128 tiles, and K = 512 fully in flight).
     {128, 64, 64, 8, 0, 1},
     {128, 64, 64, 8, 1, 1},
-    // Cluster split-K: the stages plus a 128-row FP32 receive buffer.
-    {128, 64, 64, 6, 2, 1},
-    {128, 128, 64, 4, 2, 1},
 };
 std::span<const KernelEntry> umma_entries();
 

@@ -258,8 +258,8 @@ int main(void) {
   test_watchdog(ctx);
   const char* impls[] = {NULL, "umma_128x256x64_s4", "umma_128x128x64_s6", "umma_128x256x64_s4_ksm",
                          "umma_128x128x64_s6_ksm", "umma_256x256x64_s7_c2", "umma_256x256x64_s7_c2_ksm",
-                         "umma_128x64x64_s8", "umma_128x64x64_s8_ksm", "umma_128x64x64_s6_kcl",
-                         "umma_128x128x64_s4_kcl", "gemv_256x256_ksm", "gemv_64x256_ksm", "ummav_128x16x64_s11", "ummav_128x16x64_s6x2",
+                         "umma_128x64x64_s8", "umma_128x64x64_s8_ksm",
+                         "gemv_256x256_ksm", "gemv_64x256_ksm", "ummav_128x16x64_s11", "ummav_128x16x64_s6x2",
                          "simt_64x64x16"};
   for (int bf16 = 0; bf16 < 2; ++bf16)
     for (int la = 0; la < 2; ++la)

@@ -21,7 +21,6 @@ pytestmark = pytest.mark.gpu
 
 IMPLS = ["umma_128x256x64_s4", "umma_128x128x64_s6", "umma_128x256x64_s4_ksm", "umma_128x128x64_s6_ksm",
          "umma_256x256x64_s7_c2", "umma_256x256x64_s7_c2_ksm", "umma_128x64x64_s8", "umma_128x64x64_s8_ksm",
-         "umma_128x64x64_s6_kcl", "umma_128x128x64_s4_kcl",
          "gemv_256x256_ksm", "gemv_128x256_ksm", "gemv_64x256_ksm", "gemv_32x256_ksm", "ummav_128x16x64_s11", "ummav_128x16x64_s6x2",
          "simt_64x64x16"]
 
@@ -75,7 +74,7 @@ def _aligned_case(M, N, K, la, lb, alpha, beta, batch, dtype, seed):
 @pytest.mark.parametrize("dtype", ["f16", "bf16"])
 @pytest.mark.parametrize("la,lb", [(0, 0), (0, 1), (1, 0), (1, 1)])
 @pytest.mark.parametrize("impl", ["umma_128x256x64_s4", "umma_128x128x64_s6", "umma_256x256x64_s7_c2",
-                                  "umma_128x64x64_s8", "umma_128x64x64_s6_kcl", "umma_128x128x64_s4_kcl"])
+                                  "umma_128x64x64_s8"])
 def test_umma_layouts_alpha_beta_batch(cuda, dtype, la, lb, impl):
     """Operands the TMA path can address (16-byte aligned, ld % 8 == 0): the
     tcgen05 kernel with K-major and MN-major operands, edge tiles in M, N and K."""

@@ -3,9 +3,7 @@ tests/test_splitk.cu pattern): tall-K shapes split by the SM count, 10 runs
 bitwise identical, within tolerance of the FP64 oracle; odd split counts and
 K tails; general layouts with beta; the first call for a stream inside CUDA
 graph capture is refused without breaking the capture; later calls capture
-and replay bit-identically. Cluster split-K (_kcl: the partial tiles reduced
-through distributed shared memory): every cluster size 1, 2, 4 and 8, the
-same bitwise and oracle checks, ragged tiles, layouts, alpha/beta, batch."""
+and replay bit-identically."""
 import numpy as np
 import pytest
 
@@ -17,7 +15,6 @@ pytestmark = pytest.mark.gpu
 
 SPLIT_IMPLS = ["umma_128x256x64_s4_ksm", "umma_128x128x64_s6_ksm", "umma_256x256x64_s7_c2_ksm",
                "umma_128x64x64_s8_ksm"]
-CLUSTER_IMPLS = ["umma_128x64x64_s6_kcl", "umma_128x128x64_s4_kcl"]
 
 
 @pytest.mark.parametrize("mn", [256, 512, 1024])
@@ -55,7 +52,7 @@ def test_config4_tall_k_bitwise_and_oracle(cuda, mn):
 
 @pytest.mark.parametrize("shape", [(300, 200, 30001, 0, 0, 1.0, 0.0), (129, 136, 7777, 1, 0, -0.5, 0.75),
                                    (64, 520, 20480, 0, 1, 2.0, 1.0), (9, 1000, 4099, 1, 1, 1.0, -1.0)])
-@pytest.mark.parametrize("impl", SPLIT_IMPLS + CLUSTER_IMPLS)
+@pytest.mark.parametrize("impl", SPLIT_IMPLS)
 def test_split_shapes_layouts(cuda, shape, impl):
     torch = cuda
     M, N, K, la, lb, alpha, beta = shape
@@ -75,44 +72,6 @@ def test_split_shapes_layouts(cuda, shape, impl):
         outs.append(host(dC))
     assert all(np.array_equal(o, outs[0]) for o in outs)
     check(d, A, B, C0, outs[0], op.gemm_ref(d, A, B, C0 if beta != 0 else None), f"{impl} {shape}")
-
-
-# (M, N, K, dtype): 512^3 and 1024^3 (configs 1 and 2), a short-K tile grid
-# that takes eight-CTA clusters, K tails, ragged M/N edges, a K of one block.
-CLUSTER_SHAPES = [(512, 512, 512, "f16"), (1024, 1024, 1024, "bf16"), (256, 256, 4096, "bf16"),
-                  (300, 520, 1000, "f16"), (129, 136, 7777, "bf16"), (200, 72, 64, "f16"), (64, 64, 200, "bf16")]
-
-
-@pytest.mark.parametrize("shape", CLUSTER_SHAPES)
-@pytest.mark.parametrize("impl", CLUSTER_IMPLS)
-def test_cluster_split_bitwise_and_oracle(cuda, shape, impl):
-    torch = cuda
-    M, N, K, dtype = shape
-    d = op.make_desc(M, N, K, dtype=dtype)
-    g = ac.Generator(M * 7 + N + K)
-    A, B = g.uniform(M * K, dtype), g.uniform(K * N, dtype)
-    ctx = context(torch)
-    plan = ctx.plan(M, N, K, impl, ac.DTYPE_BF16 if dtype == "bf16" else ac.DTYPE_F16)
-    assert plan["splits"] in (1, 2, 4, 8) and plan["grid"] == plan["tiles"] * plan["splits"], plan
-    assert plan["tiles"] * plan["splits"] <= 148 or plan["splits"] == 1, plan
-    dA, dB = dev(torch, A), dev(torch, B)
-    first = None
-    for _ in range(10):
-        dC = dev(torch, np.zeros(M * N, np.uint16))
-        run(torch, ctx, d, dA, dB, dC, impl)
-        out = host(dC)
-        if first is None:
-            first = out
-        else:
-            assert np.array_equal(out, first), f"{impl} {shape}: run differs from run 0"
-    check(d, A, B, None, first, op.gemm_ref(d, A, B), f"{impl} {shape} S={plan['splits']}")
-    assert op.compare(d, first, op.gemm_ref(d, A, B), None, op.tolerance(d, A, B, kind="north_star"))["pass"]
-
-
-def test_cluster_split_sizes_all_occur(cuda):
-    ctx = context(cuda)
-    sizes = {ctx.plan(M, N, K, impl)["splits"] for impl in CLUSTER_IMPLS for (M, N, K, _) in CLUSTER_SHAPES}
-    assert {1, 2, 4, 8} <= sizes, sizes
 
 
 def test_odd_split_counts_occur(cuda):
