@@ -117,6 +117,19 @@ __global__ void __launch_bounds__(GThreads, gemv_ctas_per_sm(MT)) gemv_kernel(Ge
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[m][j] = 0.f;
 
+  // The CTA's first batch of weight rows (rows k_begin .. +RG*U, its BN
+  // columns) into L2 while the previous grid on the stream ends
+  // (ptx::prefetch_l2: a hint, safe before the wait). One prefetch per 64
+  // bytes, spread over the CTA's threads independently of the load mapping.
+  if constexpr (VECB) {
+    constexpr int P = LPR >= 4 ? LPR / 4 : 1;  // 64-byte pieces per row
+    const int rows = min(RG * U, k_end - k_begin);
+#pragma unroll 1
+    for (int i = tid; i < rows * P; i += GThreads) {
+      const int col = n0 + (i % P) * 32;
+      if (col < a.N) ptx::prefetch_l2(B + (long long)(k_begin + i / P) * a.ldb + col);
+    }
+  }
   // Programmatic dependent launch: nothing global is read before the grids
   // this one depends on have completed (their writes are then visible).
   ptx::griddep_wait();

@@ -125,6 +125,25 @@ __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+// L2 prefetches. A prefetch is a hint: it changes neither memory contents nor
+// ordering, and L2 is the point of coherence for device memory, so one issued
+// before griddepcontrol.wait cannot make a later load (after the wait) see
+// stale data even if the previous grid writes those bytes. Kernels issue them
+// for their first operand blocks before that wait, so the first DRAM round
+// trip overlaps the tail of the previous grid on the stream.
+// One box of a tiled tensor map (the same coordinates and alignment rule as
+// tma_load_3d).
+__device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* map, int x, int y, int z) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+// The line holding global address p.
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(p)));
+}
+
 // ---------------------------------------------------------------- tcgen05
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)

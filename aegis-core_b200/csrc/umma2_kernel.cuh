@@ -94,6 +94,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     ptx::prefetch_tensormap(&tmA);
     ptx::prefetch_tensormap(&tmB);
+    // This CTA's half of the first unit's first k-blocks into L2 while the
+    // previous grid ends (unsplit walks only, as in umma_gemm_kernel).
+    const Unit u = decode_unit_pair<BN>(a, first_unit);
+    if (a.splits == 1)
+      prefetch_first_blocks<A_MN, B_MN, 128, BNH>(&tmA, &tmB, a.M, a.N, a.K, u.m0 + 128 * int(rank),
+                                                u.n0 + BNH * int(rank), u.kb0, min(u.nkb, STAGES),
+                                                a.a_batched ? u.b : 0, a.b_batched ? u.b : 0);
   }
   if (warp == 1) {
     ptx::tmem_alloc_pair(ptx::smem_addr(tmem_slot), L::TMEM_COLS);

@@ -139,10 +139,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::tc_fence_after();
     tmem_base = *tmem_slot;
   }
-  // Programmatic dependent launch: no global memory is touched before the
-  // grids this one depends on have completed.
-  ptx::griddep_wait();
-
   const unsigned r0 = range_start(a, blockIdx.x), r1 = range_start(a, blockIdx.x + 1);
   auto next_seg = [&](unsigned pos) {
     Seg s;
@@ -152,6 +148,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     s.nkb = int(min(unsigned(a.kb - s.kb0), r1 - pos));
     return s;
   };
+  if (warp == 0 && lane == 0) {
+    // The weights of this CTA's first STAGES k-blocks into L2 while the
+    // previous grid ends (ptx::tma_prefetch_3d: a hint, safe before the wait).
+    int n = 0;
+    for (unsigned pos = r0; pos < r1 && n < STAGES;) {
+      const Seg sg = next_seg(pos);
+      for (int i = 0; i < sg.nkb && n < STAGES; ++i, ++n) {
+        const int k0 = (sg.kb0 + i) * BK;
+        if (k0 + BK > a.K) break;  // whole boxes only (as the umma kernels)
+        if (sg.tile * BMN + 64 <= a.N) ptx::tma_prefetch_3d(&tmB, sg.tile * BMN, k0, 0);
+        if (sg.tile * BMN + 128 <= a.N) ptx::tma_prefetch_3d(&tmB, sg.tile * BMN + 64, k0, 0);
+      }
+      pos += sg.nkb;
+    }
+  }
+  // Programmatic dependent launch: no global memory is read or written before
+  // the grids this one depends on have completed.
+  ptx::griddep_wait();
 
   if (warp == 0) {
     // ------------------------------------------------ TMA producer
