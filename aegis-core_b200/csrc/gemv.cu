@@ -307,13 +307,14 @@ GPlan plan_for(int cfg, const GemmParams& p) {
   const int sms = d ? d->sm_count : 148;
   // Split K so that tiles x splits fills one wave (gemv_ctas_per_sm CTAs per
   // SM: ~128 KB of weight loads in flight per SM at MT <= 2), with at least
-  // 64 rows a split; a split's A rows should fit the shared buffer (kc * MT
-  // floats: one staging chunk), and the partials the workspace cap.
+  // 64 rows a split, and the partials within the workspace cap. A split's A
+  // rows need not fit the shared buffer: the kernel stages them in chunks
+  // (capping the split there had forced extra splits, a second wave, e.g.
+  // M = 16, K x N = 4096 x 14336 on 74 SMs).
   const long long target = (long long)sms * gemv_ctas_per_sm(pl.MT);
   long long S = std::max<long long>(1, target / pl.tiles);  // rounded down: never a second wave
   S = std::min<long long>(S, std::max(1, ceil_div(p.K, 64)));
   int kc = ceil_div(ceil_div(p.K, int(S)), 16) * 16;
-  kc = std::min(kc, (kSmemFloats / pl.MT) / 16 * 16);
   const long long slot = pl.tiles * pl.MT * c.BN * (long long)sizeof(float);
   const long long cap = std::max<long long>(1, gemm::kSplitKMaxWorkspace / std::max<long long>(1, slot));
   if (ceil_div(p.K, kc) > cap) {
