@@ -80,6 +80,8 @@ _SIGNATURES = {
     "aegis_registry_json": (c_int, [c_void_p, c_char_p, c_size_t, POINTER(c_size_t)]),
     "aegis_gemm_plan_json": (c_int, [c_void_p, c_char_p, c_int, c_int, c_int, c_int, c_char_p, c_size_t,
                                      POINTER(c_size_t)]),
+    "aegis_plan_simulated_json": (c_int, [c_int, c_int, c_char_p, c_int, c_int, c_int, c_int, c_char_p, c_size_t,
+                                          POINTER(c_size_t)]),
     "aegis_gemv_noalloc": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_float, c_void_p, c_int64,
                                    c_void_p, c_int64, c_float, c_void_p, c_int64]),
     "aegis_watchdog_selftest": (c_int, [c_void_p, c_int64]),
@@ -130,6 +132,16 @@ def _query_string(fn, *args) -> str:
     buf = ctypes.create_string_buffer(needed.value)
     check(fn(*args, buf, needed.value, ctypes.byref(needed)), fn.__name__)
     return buf.value.decode()
+
+
+def plan_simulated(M: int, N: int, K: int, impl: str | None = None, dtype: int = DTYPE_F16, arch: int = 100,
+                   sm_count: int = 148) -> dict:
+    """The dispatcher's choice and the launch plan on a simulated device (no
+    GPU needed): {"impl", "splits", "k_chunk", "tiles", "grid", "dispatch",
+    "kind"} (aegis_plan_simulated_json)."""
+    lib = load()
+    return json.loads(_query_string(lib.aegis_plan_simulated_json, arch, sm_count,
+                                    impl.encode() if impl else None, dtype, M, N, K))
 
 
 class Context:

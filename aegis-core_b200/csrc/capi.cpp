@@ -17,6 +17,7 @@
 #include "aegis/matmul.h"
 #include "capi_error.h"
 #include "common.cuh"
+#include "device.h"
 #include "kernels.h"
 #include "status.h"
 
@@ -401,6 +402,47 @@ int aegis_gemm_plan_json(aegis_context* ctx, const char* impl, int dtype, int M,
   char b[256];
   std::snprintf(b, sizeof b, "{\"impl\":\"%s\",\"splits\":%d,\"k_chunk\":%d,\"tiles\":%lld,\"grid\":%u}", name,
                 pl.splits, pl.k_chunk, pl.tiles, pl.grid);
+  return copy_out(b, buf, buf_len, needed);
+}
+
+int aegis_plan_simulated_json(int arch, int sm_count, const char* impl, int dtype, int M, int N, int K, char* buf,
+                              size_t buf_len, size_t* needed) {
+  const char* fn = "aegis_plan_simulated_json";
+  if (M <= 0 || N <= 0 || K <= 0) return fail_arg(fn, "M, N and K must be positive");
+  if (dtype != AEGIS_DTYPE_F16 && dtype != AEGIS_DTYPE_BF16) return fail_arg(fn, "bad dtype");
+  if (arch <= 0 || sm_count <= 0 || sm_count > 4096) return fail_arg(fn, "arch and sm_count must be positive");
+  // B200's limits (cudaDeviceProp of the part), with the given arch and SM count.
+  aegis::hw::DeviceLimits sim;
+  sim.name = "simulated";
+  sim.arch = arch;
+  sim.sm_count = sm_count;
+  sim.smem_per_sm = 233472;
+  sim.smem_per_block = 49152;
+  sim.smem_per_block_optin = 232448;
+  sim.regs_per_sm = 65536;
+  sim.regs_per_block = 65536;
+  sim.max_threads_per_sm = 2048;
+  sim.max_threads_per_block = 1024;
+  sim.l2_bytes = size_t(126) << 20;
+  sim.global_mem_bytes = size_t(183359) << 20;
+  const aegis::hw::ScopedSimulation scope(sim);
+  static const char dummy[16] alignas(16) = {};
+  const aegis::gemm::GemmParams p = aegis::gemm::row_major_params(
+      dummy, dummy, const_cast<char*>(dummy), M, N, K,
+      dtype == AEGIS_DTYPE_BF16 ? aegis::gemm::DType::BF16 : aegis::gemm::DType::F16);
+  const aegis::gemm::DeviceCaps caps = aegis::gemm::current_caps();
+  const aegis::detail::Choice c = aegis::detail::choose(aegis::detail::winners_table(), p, caps);
+  const char* chosen = c.kernel ? c.kernel->name : "none";
+  const char* name = impl ? impl : chosen;
+  if (!aegis::gemm::find(name)) return fail_arg(fn, "no such kernel configuration in the registry");
+  aegis::gemm::LaunchPlan pl;
+  if (!aegis::gemm::launch_plan(name, p, &pl)) pl = aegis::gemm::LaunchPlan{};
+  char b[384];
+  std::snprintf(b, sizeof b,
+                "{\"impl\":\"%s\",\"splits\":%d,\"k_chunk\":%d,\"tiles\":%lld,\"grid\":%u,\"dispatch\":\"%s\","
+                "\"kind\":\"%s\"}",
+                name, pl.splits, pl.k_chunk, pl.tiles, pl.grid, chosen,
+                c.kind == aegis::detail::Choice::Kind::Aegis ? "winner" : "rule");
   return copy_out(b, buf, buf_len, needed);
 }
 

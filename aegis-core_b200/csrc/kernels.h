@@ -35,7 +35,9 @@ gemm::LaunchPlan gemv_plan(int cfg, const gemm::GemmParams& p);
 cudaError_t gemv_attrs(int cfg, cudaFuncAttributes* attrs);
 
 // ummav family: decode GEMM on tensor cores (swap-AB, stream-K segments).
-// Runs the CUDA-core gemv for problems it cannot take (ummav_applicable).
+// Runs the CUDA-core gemv for problems it cannot take (ummav_applicable: an
+// sm_100 device and a problem ummav_takes).
+bool ummav_takes(const gemm::GemmParams& p);  // shape, layout and alignment only
 bool ummav_applicable(const gemm::GemmParams& p);
 cudaError_t ummav_run(int cfg, const gemm::GemmParams& p, cudaStream_t stream);
 gemm::LaunchPlan ummav_plan(int cfg, const gemm::GemmParams& p);

@@ -67,7 +67,7 @@ const gemm::KernelEntry* rule_for(const gemm::GemmParams& p, const gemm::DeviceC
     // it takes row-major operands the TMA path can address, the CUDA-core GEMV
     // everything else.
     if (p.M <= 2) return by_name("gemv_256x256_ksm");
-    if (caps.arch == 100 && ummav_applicable(p)) return by_name("ummav_128x16x64_s6x2");
+    if (caps.arch == 100 && ummav_takes(p)) return by_name("ummav_128x16x64_s6x2");
     if (p.M <= 8) return by_name("gemv_128x256_ksm");
     return by_name("gemv_64x256_ksm");
   }

@@ -408,10 +408,14 @@ cudaError_t launch(int stages, const CUtensorMap& ta, const CUtensorMap& tb, con
 
 }  // namespace ummav
 
+bool ummav_takes(const gemm::GemmParams& p) {
+  return p.M <= ummav::MPAD && p.batch == 1 && p.layout_a == gemm::Layout::RowMajor &&
+         p.layout_b == gemm::Layout::RowMajor && gemm::tma_compatible(p);
+}
+
 bool ummav_applicable(const gemm::GemmParams& p) {
   const hw::DeviceLimits* d = hw::physical();
-  return d && d->arch == 100 && p.M <= ummav::MPAD && p.batch == 1 && p.layout_a == gemm::Layout::RowMajor &&
-         p.layout_b == gemm::Layout::RowMajor && gemm::tma_compatible(p);
+  return d && d->arch == 100 && ummav_takes(p);
 }
 
 cudaError_t ummav_run(int cfg, const gemm::GemmParams& p, cudaStream_t stream) {

@@ -255,6 +255,19 @@ AEGIS_API int aegis_registry_json(aegis_context* ctx, char* buf, size_t buf_len,
 AEGIS_API int aegis_gemm_plan_json(aegis_context* ctx, const char* impl, int dtype, int M, int N, int K, char* buf,
                                    size_t buf_len, size_t* needed);
 
+/* aegis_gemm_plan_json without a device or a context: the dispatcher's choice
+ * and the launch plan for a packed row-major problem on a simulated device of
+ * compute capability `arch` (major*10 + minor; 100 for B200) with `sm_count`
+ * SMs and B200's other limits. JSON as aegis_gemm_plan_json plus
+ * "kind":"winner" (a tuned winners row chose it) or "rule" (the built-in
+ * rule), and "dispatch" (the chosen kernel; `impl` only replaces the kernel
+ * whose plan is reported). Runs nothing on any GPU; for planning tools and
+ * tests of the dispatch rules on machines without one. No reference
+ * counterpart (the reference tests dispatch on its device only,
+ * tests/test_matmul.cu). */
+AEGIS_API int aegis_plan_simulated_json(int arch, int sm_count, const char* impl, int dtype, int M, int N, int K,
+                                        char* buf, size_t buf_len, size_t* needed);
+
 /* ---- ABI 1.4 addition: decode GEMV that allocates nothing -------------------
  * C = alpha * A * B + beta * C for decode shapes, like aegis_gemm_*_ex with
  * row- or column-major A and B (layout_a, layout_b), one batch, M <= 16 and

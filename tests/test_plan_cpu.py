@@ -1,0 +1,167 @@
+"""Dispatch rules and launch plans on a simulated B200, without a GPU
+(aegis_plan_simulated_json).
+
+The reference tests its dispatcher on its device (tests/test_matmul.cu); here
+the same host logic runs against a simulated device profile:
+  - every row of the tuned winners header is chosen for its exact shape;
+  - other M with a tuned (N, K) take the nearest M in log2, ties to the larger
+    M (reference src/matmul.cu:432-467, include/aegis/matmul.h:8-45);
+  - untuned (N, K) fall back to the built-in rule (decode / TMA-addressable /
+    general kernel), and no winners row is used on a device that is not sm_100;
+  - GEMV plans stay one wave of resident CTAs, split-K plans cover K with no
+    empty split, ummav plans fit the SMs, all as functions of the SM count.
+"""
+import math
+import os
+import re
+
+import pytest
+
+import aegis_capi as ac
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "aegis", "winners", "sm_100a.h")
+BF16 = ac.DTYPE_BF16
+
+
+def winner_rows():
+    rows = []
+    for line in open(HEADER):
+        m = re.match(r'\s*\{(\d+), (\d+), (\d+), "([^"]+)"', line)
+        if m:
+            rows.append((int(m.group(1)), int(m.group(2)), int(m.group(3)), m.group(4)))
+    return rows
+
+
+def plan(M, N, K, impl=None, sms=148, arch=100):
+    return ac.plan_simulated(M, N, K, impl=impl, dtype=BF16, arch=arch, sm_count=sms)
+
+
+def test_header_has_rows():
+    assert len(winner_rows()) >= 17
+
+
+@pytest.mark.parametrize("row", winner_rows(), ids=lambda r: f"{r[0]}x{r[1]}x{r[2]}")
+def test_winner_rows_are_chosen_for_their_shape(row):
+    M, N, K, impl = row
+    p = plan(M, N, K)
+    assert p["kind"] == "winner" and p["dispatch"] == impl and p["impl"] == impl, p
+
+
+def nearest(rows, M, N, K):
+    """The nearest-M rule restated: same (N, K), smallest |log2 M' - log2 M|
+    (an exact M first), ties to the larger M'."""
+    best = None
+    for (m, n, k, impl) in rows:
+        if (n, k) != (N, K):
+            continue
+        d = -1.0 if m == M else abs(math.log2(m) - math.log2(M))
+        if best is None or d < best[0] or (d == best[0] and m > best[1]):
+            best = (d, m, impl)
+    return best[2] if best else None
+
+
+@pytest.mark.parametrize("M", [2, 3, 6, 8, 12, 24, 64, 200, 1000, 3000, 6000, 12000])
+def test_nearest_m_for_tuned_n_k(M):
+    rows = winner_rows()
+    for (N, K) in sorted({(n, k) for (_, n, k, _) in rows}):
+        want = nearest(rows, M, N, K)
+        p = plan(M, N, K)
+        assert p["kind"] == "winner" and p["dispatch"] == want, (M, N, K, p)
+
+
+@pytest.mark.parametrize("shape,kernel", [
+    ((1, 1000, 3000), "gemv_256x256_ksm"),            # M <= 2: CUDA-core weight stream
+    ((2, 1000, 3000), "gemv_256x256_ksm"),
+    ((8, 1000, 3000), "ummav_128x16x64_s6x2"),        # 2 < M <= 16, TMA-addressable
+    ((16, 1000, 3000), "ummav_128x16x64_s6x2"),
+    ((8, 1001, 3000), "gemv_128x256_ksm"),            # ldb not a multiple of 8: no TMA
+    ((12, 1001, 3000), "gemv_64x256_ksm"),
+    ((2000, 120, 3000), "umma_128x128x64_s6_ksm"),    # N <= 128
+    ((100, 2000, 3000), "umma_128x256x64_s4_ksm"),    # M <= 128
+    ((2000, 2000, 3000), "umma_256x256x64_s7_c2_ksm"),
+    ((2000, 2001, 3000), "simt_64x64x16"),            # not TMA-addressable
+])
+def test_built_in_rule_for_untuned_shapes(shape, kernel):
+    p = plan(*shape)
+    assert p["kind"] == "rule" and p["dispatch"] == kernel, (shape, p)
+
+
+def test_no_winner_rows_off_sm100():
+    for (M, N, K, _) in winner_rows():
+        p = plan(M, N, K, arch=90)
+        assert p["kind"] == "rule", p
+        if M > 16:
+            assert p["dispatch"] == "simt_64x64x16", p
+
+
+DECODE = [(m, n, k) for m in (1, 2, 4, 8, 16) for (n, k) in ((4096, 4096), (14336, 4096), (4096, 14336))]
+GEMV_CTAS_PER_SM = {1: 4, 2: 4, 4: 4, 8: 2, 16: 1}  # by row tile MT (gemv.cu gemv_ctas_per_sm)
+
+
+@pytest.mark.parametrize("sms", [148, 132, 74])
+@pytest.mark.parametrize("impl", ["gemv_256x256_ksm", "gemv_128x256_ksm", "gemv_64x256_ksm", "gemv_32x256_ksm"])
+def test_gemv_plans_are_one_wave(impl, sms):
+    bn = int(impl.split("_")[1].split("x")[0])
+    for (M, N, K) in DECODE:
+        mt = 1
+        while mt < M and mt < 16 and mt < 1024 // bn:
+            mt *= 2
+        p = plan(M, N, K, impl, sms=sms)
+        assert p["grid"] <= GEMV_CTAS_PER_SM[mt] * sms or p["splits"] == 1, (M, N, K, sms, p)
+        assert (p["splits"] - 1) * p["k_chunk"] < K <= p["splits"] * p["k_chunk"], (M, N, K, p)
+
+
+SPLIT_IMPLS = {"umma_128x256x64_s4_ksm": 1, "umma_128x128x64_s6_ksm": 1, "umma_256x256x64_s7_c2_ksm": 2,
+               "umma_128x64x64_s8_ksm": 1}
+TALL_K = [(256, 256, 65536), (512, 512, 65536), (1024, 1024, 65536), (300, 200, 30001), (129, 136, 7777),
+          (16, 4096, 14336), (1, 14336, 4096)]
+
+
+@pytest.mark.parametrize("sms", [148, 74])
+@pytest.mark.parametrize("impl", list(SPLIT_IMPLS))
+def test_split_k_plans_cover_k_without_empty_splits(impl, sms):
+    ctas = SPLIT_IMPLS[impl]
+    for (M, N, K) in TALL_K:
+        p = plan(M, N, K, impl, sms=sms)
+        assert p == plan(M, N, K, impl, sms=sms)  # a pure function of shape and device
+        S, kc = p["splits"], p["k_chunk"]
+        assert S >= 1 and kc % 64 == 0, p
+        assert (S - 1) * kc < K <= S * kc, (M, N, K, p)
+        assert p["grid"] == p["tiles"] * S * ctas, p
+
+
+def test_tall_k_shapes_split_when_tiles_cannot_fill_the_sms():
+    for (M, N, K) in [(256, 256, 65536), (512, 512, 65536)]:
+        for impl, ctas in SPLIT_IMPLS.items():
+            p = plan(M, N, K, impl)
+            assert p["splits"] > 1, (M, N, K, p)
+
+
+def test_unsplit_configs_never_split():
+    for impl in ["umma_128x256x64_s4", "umma_128x128x64_s6", "umma_256x256x64_s7_c2", "umma_128x64x64_s8"]:
+        for (M, N, K) in TALL_K:
+            assert plan(M, N, K, impl)["splits"] == 1
+
+
+@pytest.mark.parametrize("sms", [148, 132])
+@pytest.mark.parametrize("impl,per_sm", [("ummav_128x16x64_s11", 1), ("ummav_128x16x64_s6x2", 2)])
+def test_ummav_plans_fit_the_sms(impl, per_sm, sms):
+    for (M, N, K) in DECODE:
+        p = plan(M, N, K, impl, sms=sms)
+        kb = math.ceil(K / 64)
+        assert p["tiles"] == math.ceil(N / 128), p
+        assert 1 <= p["grid"] <= min(per_sm * sms, p["tiles"] * kb), p
+
+
+def test_arguments_are_checked():
+    for bad in [dict(M=0, N=8, K=8), dict(M=8, N=-1, K=8)]:
+        with pytest.raises(ac.AegisError) as e:
+            ac.plan_simulated(**bad)
+        assert e.value.status == ac.AEGIS_ERR_INVALID_ARGUMENT
+    with pytest.raises(ac.AegisError):
+        ac.plan_simulated(8, 8, 8, impl="no_such_kernel")
+    with pytest.raises(ac.AegisError):
+        ac.plan_simulated(8, 8, 8, sm_count=0)
+    with pytest.raises(ac.AegisError):
+        ac.plan_simulated(8, 8, 8, dtype=7)
