@@ -135,8 +135,8 @@ __global__ void __launch_bounds__(GThreads, gemv_ctas_per_sm(MT)) gemv_kernel(Ge
   ptx::griddep_wait();
 
   // This CTA's A rows, staged as FP32 [k][MT] in chunks of the shared buffer
-  // (one chunk for every plan the planner makes unless M and the split are
-  // both large); each chunk's weights stream in batches of U rows per
+  // (8192 / MT rows each; one chunk when the K slice fits); each chunk's
+  // weights stream in batches of U rows per
   // thread: all U loads of a batch are issued before any of its math, and no
   // barrier sits inside the batch loop, so the warps of the CTA (and the
   // other CTAs on the SM) keep loads in flight while one warp computes.
