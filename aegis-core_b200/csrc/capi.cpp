@@ -63,7 +63,8 @@ int enter(aegis_context* ctx, const char* fn) {
 int run_gemm(aegis_context* ctx, const aegis::gemm::GemmParams& p, const char* fn) {
   if (int s = enter(ctx, fn)) return s;
   if (aegis::gemm::validate(p) != cudaSuccess)
-    return fail_arg(fn, "negative size, too-small leading dimension, null operand, bad layout or overlapping C batches");
+    return fail_arg(fn, "negative size or a size above 2^31 - 2^20, too-small leading dimension, null operand, "
+                        "bad layout or overlapping C batches");
   if (aegis::gemm::is_empty(p)) return AEGIS_OK;
   const cudaError_t e = aegis::matmul(p, ctx->stream);
   if (e == cudaSuccess) return AEGIS_OK;
@@ -355,7 +356,8 @@ int aegis_gemm_impl(aegis_context* ctx, const char* impl, int dtype, int layout_
   p.stride_a = stride_a; p.stride_b = stride_b; p.stride_c = stride_c;
   p.dtype = dtype == AEGIS_DTYPE_BF16 ? aegis::gemm::DType::BF16 : aegis::gemm::DType::F16;
   if (aegis::gemm::validate(p) != cudaSuccess)
-    return fail_arg(fn, "negative size, too-small leading dimension, null operand, bad layout or overlapping C batches");
+    return fail_arg(fn, "negative size or a size above 2^31 - 2^20, too-small leading dimension, null operand, "
+                        "bad layout or overlapping C batches");
   if (aegis::gemm::is_empty(p)) return AEGIS_OK;
   const cudaError_t err = e->run(p, ctx->stream);
   if (err == cudaSuccess) return AEGIS_OK;
@@ -389,6 +391,8 @@ int aegis_gemm_plan_json(aegis_context* ctx, const char* impl, int dtype, int M,
                          size_t buf_len, size_t* needed) {
   const char* fn = "aegis_gemm_plan_json";
   if (M <= 0 || N <= 0 || K <= 0) return fail_arg(fn, "M, N and K must be positive");
+  if (M > aegis::gemm::kMaxDim || N > aegis::gemm::kMaxDim || K > aegis::gemm::kMaxDim)
+    return fail_arg(fn, "M, N and K must be at most 2^31 - 2^20");
   if (dtype != AEGIS_DTYPE_F16 && dtype != AEGIS_DTYPE_BF16) return fail_arg(fn, "bad dtype");
   if (int s = enter(ctx, fn)) return s;
   static const char dummy[16] alignas(16) = {};
@@ -409,6 +413,8 @@ int aegis_plan_simulated_json(int arch, int sm_count, const char* impl, int dtyp
                               size_t buf_len, size_t* needed) {
   const char* fn = "aegis_plan_simulated_json";
   if (M <= 0 || N <= 0 || K <= 0) return fail_arg(fn, "M, N and K must be positive");
+  if (M > aegis::gemm::kMaxDim || N > aegis::gemm::kMaxDim || K > aegis::gemm::kMaxDim)
+    return fail_arg(fn, "M, N and K must be at most 2^31 - 2^20");
   if (dtype != AEGIS_DTYPE_F16 && dtype != AEGIS_DTYPE_BF16) return fail_arg(fn, "bad dtype");
   if (arch <= 0 || sm_count <= 0 || sm_count > 4096) return fail_arg(fn, "arch and sm_count must be positive");
   // B200's limits (cudaDeviceProp of the part), with the given arch and SM count.

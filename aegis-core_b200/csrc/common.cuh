@@ -8,8 +8,10 @@
 
 namespace aegis {
 
+// ceil(a / b) for a >= 0, b > 0, without the overflow of (a + b - 1) / b near
+// the type's maximum (an M or N of 2^31 - 1 is a valid problem).
 template <class T>
-__host__ __device__ constexpr T ceil_div(T a, T b) { return (a + b - 1) / b; }
+__host__ __device__ constexpr T ceil_div(T a, T b) { return a / b + (a % b != 0 ? 1 : 0); }
 
 // 16-bit element traits: f16 and bf16 share every kernel; only the
 // conversions differ.

@@ -105,7 +105,7 @@ __global__ void __launch_bounds__(GThreads, gemv_ctas_per_sm(MT)) gemv_kernel(Ge
   const long long b = a.batch0 + blockIdx.z;
   const int n0 = nt * BN, m0 = mt * MT;
   const int k_begin = split * a.kc;
-  const int k_end = min(a.K, k_begin + a.kc);
+  const int k_end = k_begin + min(a.kc, a.K - k_begin);  // no k_begin + kc overflow near 2^31
   const T* A = static_cast<const T*>(a.A) + b * a.sa;
   const T* B = static_cast<const T*>(a.B) + b * a.sb;
   const int n = n0 + l * 8;  // first of this thread's 8 columns
@@ -314,13 +314,16 @@ GPlan plan_for(int cfg, const GemmParams& p) {
   const long long target = (long long)sms * gemv_ctas_per_sm(pl.MT);
   long long S = std::max<long long>(1, target / pl.tiles);  // rounded down: never a second wave
   S = std::min<long long>(S, std::max(1, ceil_div(p.K, 64)));
-  int kc = ceil_div(ceil_div(p.K, int(S)), 16) * 16;
+  // Rows per split: ceil(K / S) rounded up to 16, in 64-bit (K may be near
+  // 2^31); a split of all of K when rounding would pass K.
+  auto rows_for = [&](long long splits) {
+    const long long kc = ceil_div(ceil_div<long long>(p.K, splits), 16ll) * 16;
+    return int(std::min<long long>(kc, p.K));
+  };
+  int kc = rows_for(S);
   const long long slot = pl.tiles * pl.MT * c.BN * (long long)sizeof(float);
   const long long cap = std::max<long long>(1, gemm::kSplitKMaxWorkspace / std::max<long long>(1, slot));
-  if (ceil_div(p.K, kc) > cap) {
-    // Fewer, longer splits: only reachable when the shared buffer allows it.
-    kc = ceil_div(ceil_div(p.K, int(cap)), 16) * 16;
-  }
+  if (ceil_div(p.K, kc) > cap) kc = rows_for(cap);  // fewer, longer splits: the partials' workspace cap
   pl.S = ceil_div(p.K, kc);
   pl.kc = kc;
   return pl;
@@ -524,8 +527,8 @@ cudaError_t gemv_run_noalloc(const GemmParams& p, cudaStream_t stream, const cha
   const long long slot_bytes = pl.tiles * pl.MT * (8 * pl.LPR) * (long long)sizeof(float);
   if ((long long)pl.S * slot_bytes > (long long)kNoAllocPartialBytes) {
     // Fewer, longer splits so the partials fit the fixed array.
-    const int s_fit = int(std::max<long long>(1, (long long)kNoAllocPartialBytes / slot_bytes));
-    pl.kc = ceil_div(ceil_div(p.K, s_fit), 16) * 16;
+    const long long s_fit = std::max<long long>(1, (long long)kNoAllocPartialBytes / slot_bytes);
+    pl.kc = int(std::min<long long>(ceil_div(ceil_div<long long>(p.K, s_fit), 16ll) * 16, p.K));
     pl.S = ceil_div(p.K, pl.kc);
   }
 

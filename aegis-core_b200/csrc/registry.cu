@@ -19,6 +19,7 @@ namespace aegis::gemm {
 
 cudaError_t validate(const GemmParams& p) {
   if (p.M < 0 || p.N < 0 || p.K < 0 || p.batch < 0) return cudaErrorInvalidValue;
+  if (p.M > kMaxDim || p.N > kMaxDim || p.K > kMaxDim) return cudaErrorInvalidValue;
   if (is_empty(p)) return cudaSuccess;  // nothing read or written
   if (!p.A || !p.B || !p.C) return cudaErrorInvalidValue;
   if (p.dtype != DType::F16 && p.dtype != DType::BF16) return cudaErrorInvalidValue;

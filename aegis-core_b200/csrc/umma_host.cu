@@ -318,7 +318,7 @@ gemm::LaunchPlan umma_plan(int cfg, const GemmParams& p) {
   const Plan pl = make_plan(cfg, p);
   gemm::LaunchPlan r;
   r.splits = pl.splits;
-  r.k_chunk = pl.kb_per_split * umma::BK;
+  r.k_chunk = int(std::min<long long>((long long)pl.kb_per_split * umma::BK, p.K));
   r.tiles = pl.tiles;
   r.grid = unsigned(pl.grid);
   return r;

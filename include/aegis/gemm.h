@@ -58,7 +58,11 @@ inline GemmParams row_major_params(const void* A, const void* B, void* C, int M,
 
 // cudaSuccess, or cudaErrorInvalidValue for negative sizes, null operands with
 // nonzero sizes, a bad layout/dtype, ld below the contiguous extent, negative
-// A/B batch strides or overlapping C batches (reference registry.cu:13-30).
+// A/B batch strides or overlapping C batches (reference registry.cu:13-30);
+// and, beyond the reference, for M, N or K above kMaxDim, which leaves the
+// kernels' 32-bit index arithmetic (row and k loops that step past the end)
+// headroom below 2^31.
+inline constexpr int kMaxDim = (1 << 30) + ((1 << 30) - (1 << 20));  // 2^31 - 2^20
 cudaError_t validate(const GemmParams& p);
 inline bool is_empty(const GemmParams& p) {
   return p.M == 0 || p.N == 0 || p.K == 0 || p.batch == 0;

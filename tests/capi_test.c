@@ -88,6 +88,9 @@ static void test_errors(aegis_context* ctx) {
   EXPECT(aegis_gemm_f16_strided_batched(ctx, 0, 0, 4, 4, 4, 1.f, p, 4, 16, p, 4, 16, 0.f, p, 4, 8, 2) ==
              AEGIS_ERR_INVALID_ARGUMENT, "overlapping C batches");
   EXPECT(aegis_gemm_f16(NULL, p, p, p, 4, 4, 4) == AEGIS_ERR_INVALID_ARGUMENT, "ctx = NULL");
+  /* Sizes above 2^31 - 2^20 are refused before anything is read (index headroom). */
+  EXPECT(aegis_gemm_f16(ctx, p, p, p, 2147483647, 8, 8) == AEGIS_ERR_INVALID_ARGUMENT, "M = 2^31 - 1");
+  EXPECT(aegis_gemm_bf16(ctx, p, p, p, 8, 8, 2147483000) == AEGIS_ERR_INVALID_ARGUMENT, "K near 2^31");
   EXPECT(aegis_gemm_impl(ctx, "no_such_kernel", AEGIS_DTYPE_F16, 0, 0, 4, 4, 4, 1.f, p, 4, 0, p, 4, 0, 0.f, p, 4,
                          0, 1) == AEGIS_ERR_INVALID_ARGUMENT, "unknown impl");
   EXPECT(aegis_device_free(ctx, p) == AEGIS_OK, "free");

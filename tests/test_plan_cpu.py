@@ -126,7 +126,7 @@ def test_split_k_plans_cover_k_without_empty_splits(impl, sms):
         p = plan(M, N, K, impl, sms=sms)
         assert p == plan(M, N, K, impl, sms=sms)  # a pure function of shape and device
         S, kc = p["splits"], p["k_chunk"]
-        assert S >= 1 and kc % 64 == 0, p
+        assert S >= 1 and (S == 1 or kc % 64 == 0), p
         assert (S - 1) * kc < K <= S * kc, (M, N, K, p)
         assert p["grid"] == p["tiles"] * S * ctas, p
 
@@ -152,6 +152,40 @@ def test_ummav_plans_fit_the_sms(impl, per_sm, sms):
         kb = math.ceil(K / 64)
         assert p["tiles"] == math.ceil(N / 128), p
         assert 1 <= p["grid"] <= min(per_sm * sms, p["tiles"] * kb), p
+
+
+MAX_DIM = (1 << 31) - (1 << 20)  # gemm::kMaxDim
+FAMILIES = ["umma_128x256x64_s4", "umma_128x128x64_s6", "umma_128x256x64_s4_ksm", "umma_128x128x64_s6_ksm",
+            "umma_256x256x64_s7_c2", "umma_256x256x64_s7_c2_ksm", "umma_128x64x64_s8", "umma_128x64x64_s8_ksm",
+            "gemv_256x256_ksm", "gemv_128x256_ksm", "gemv_64x256_ksm", "gemv_32x256_ksm", "ummav_128x16x64_s11",
+            "ummav_128x16x64_s6x2"]
+
+
+def test_random_plans_keep_their_invariants():
+    """Seeded random shapes up to the size limit, every planner and SM count:
+    positive tiles and grids below 2^32, and for the umma and gemv families
+    K chunks that cover K with no empty split (no 32-bit overflow anywhere)."""
+    import random
+    rnd = random.Random(20261202)
+    sizes = [1, 2, 3, 15, 16, 17, 64, 65, 100, 1000, 4096, 14336, 65536, 1 << 20, MAX_DIM - 1, MAX_DIM]
+    for _ in range(3000):
+        M, N, K = [rnd.choice(sizes + [rnd.randint(1, 1 << 24), rnd.randint(1, MAX_DIM)]) for _ in range(3)]
+        impl = rnd.choice(FAMILIES + [None])
+        p = plan(M, N, K, impl, sms=rnd.choice([148, 132, 74, 16, 1]))
+        if p["impl"].startswith("simt"):
+            continue  # the general kernel has no split plan
+        assert p["splits"] >= 1 and p["tiles"] >= 1 and 1 <= p["grid"] < 2 ** 32, (M, N, K, p)
+        if p["impl"].startswith(("umma_", "gemv_")):
+            S, kc = p["splits"], p["k_chunk"]
+            assert 0 < kc <= K and (S - 1) * kc < K <= S * kc, (M, N, K, p)
+
+
+def test_sizes_above_the_limit_are_refused():
+    for shape in [(MAX_DIM + 1, 8, 8), (8, MAX_DIM + 1, 8), (8, 8, (1 << 31) - 1)]:
+        with pytest.raises(ac.AegisError) as e:
+            ac.plan_simulated(*shape)
+        assert e.value.status == ac.AEGIS_ERR_INVALID_ARGUMENT
+    assert plan(MAX_DIM, 8, 8)["tiles"] >= 1
 
 
 def test_arguments_are_checked():
