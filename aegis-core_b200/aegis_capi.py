@@ -13,7 +13,7 @@ from __future__ import annotations
 import ctypes
 import json
 import os
-from ctypes import (POINTER, c_char_p, c_double, c_float, c_int, c_int64, c_size_t, c_uint, c_void_p)
+from ctypes import (POINTER, c_char_p, c_float, c_int, c_int64, c_size_t, c_uint, c_void_p)
 
 import numpy as np
 
