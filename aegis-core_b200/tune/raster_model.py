@@ -18,10 +18,13 @@ A/B reads, against 9.6-10.4 GB measured by ncu (dram__bytes_read.sum). The
 measured ordering of group sizes (4 and 16 worse than 8) is reproduced.
 
 The model then ranks K-direction alternation (a tile walks its k-blocks
-last to first). With odd global column tiles reversed, it predicts 6.8 GB at
-126 MB of L2 and 10.0 GB at 63 MB. The forward order's prediction hardly
-depends on L2 capacity, so only a measurement can decide. A tuning aid; nothing
-in the library imports it.
+last to first), at 126 MB / 63 MB of L2:
+  - odd column tiles reversed: 6.8 GB / 10.0 GB;
+  - odd waves reversed (runs of `slots` tiles of the raster): 6.8 GB / 7.9 GB;
+  - the same wave rule in global tile coordinates: 7.2 GB / 8.8 GB.
+The forward order's prediction hardly depends on L2 capacity, so only a
+measurement can decide. `--l2-mb 63` gives the second column. A tuning aid;
+nothing in the library imports it.
 """
 from __future__ import annotations
 
@@ -97,10 +100,16 @@ def main(argv=None) -> int:
     a = p.parse_args(argv)
     t = -(-a.size // a.tile)
     kb = -(-a.size // 64)
+    W = a.slots
     cases = [(f"grouped g={g}", order_grouped(t, t, g), None) for g in (4, 8, 16)]
     o8 = order_grouped(t, t, 8)
     cases += [("g=8, odd n reversed", o8, lambda ti, m, n: n % 2 == 1),
-              ("g=8, odd m reversed", o8, lambda ti, m, n: m % 2 == 1)]
+              ("g=8, odd m reversed", o8, lambda ti, m, n: m % 2 == 1),
+              # odd waves (runs of `slots` consecutive tiles of the raster) reversed
+              ("g=8, by wave", o8, lambda ti, m, n: (ti // W) % 2 == 1),
+              # the same rule in global tile coordinates (independent of N-sharding)
+              ("g=8, by wave, global", o8, lambda ti, m, n: (((m // 8) * t * 8 + n * 8) // W) % 2 == 1),
+              ("g=12, by wave", order_grouped(t, t, 12), lambda ti, m, n: (ti // W) % 2 == 1)]
     for name, order, rev in cases:
         r = simulate(order, kb, a.slots, a.l2_mb, a.jitter, reverse=rev)
         print(f"{name:22s} A/B reads {r['ab_read_gb']:6.2f} GB   C {r['c_gb']:.2f} GB", flush=True)
