@@ -2,6 +2,7 @@
 // reference's src/matmul.cu:386-467 (validate -> empty -> alpha == 0 ->
 // choose -> KernelEntry::run) without a vendor-library path: every choice is
 // one of this library's kernels.
+#include <algorithm>
 #include <cmath>
 #include <mutex>
 #include <string>
@@ -9,6 +10,7 @@
 
 #include "aegis/gemm.h"
 #include "aegis/matmul.h"
+#include "common.cuh"
 #include "device.h"
 #include "kernels.h"
 
@@ -60,25 +62,39 @@ const gemm::KernelEntry* by_name(const char* name) {
 namespace detail {
 
 const gemm::KernelEntry* rule_for(const gemm::GemmParams& p, const gemm::DeviceCaps& caps) {
+  // The rule for shapes with no tuned row for their (N, K), from the B200
+  // tuner runs of the BASELINE shapes (aegis-core_b200/tune/runs/):
+  const bool tma = gemm::tma_compatible(p) && caps.arch == 100;
   if (p.M <= 16) {
-    // Decode. M <= 2: the CUDA-core weight stream (gemv_256x256_ksm) measured
-    // fastest at M = 1 on every BASELINE decode shape. From M = 4 the FP32 FMA
-    // work (M per weight element) makes the tensor-core stream (ummav) faster;
-    // it takes row-major operands the TMA path can address, the CUDA-core GEMV
-    // everything else.
+    // Decode. M <= 2: the CUDA-core weight stream (the gemv configs within 3%
+    // of each other and of the best at M = 1). M <= 8: the tensor-core
+    // stream ummav (fastest at M = 4). M <= 16: split-K on 128 x 128 tiles
+    // (fastest at M = 16 on all three decode shapes; ummav 1.09-1.30x
+    // slower). Operands the TMA path cannot address: the CUDA-core GEMV.
     if (p.M <= 2) return by_name("gemv_256x256_ksm");
-    if (caps.arch == 100 && ummav_takes(p)) return by_name("ummav_128x16x64_s6x2");
-    if (p.M <= 8) return by_name("gemv_128x256_ksm");
-    return by_name("gemv_64x256_ksm");
+    if (p.M <= 8) {
+      if (caps.arch == 100 && ummav_takes(p)) return by_name("ummav_128x16x64_s6x2");
+      return by_name("gemv_128x256_ksm");
+    }
+    return tma ? by_name("umma_128x128x64_s6_ksm") : by_name("gemv_64x256_ksm");
   }
-  if (gemm::tma_compatible(p) && caps.arch == 100) {
-    // CTA pairs (256 x 256 tiles) measured fastest from 4096^2 up; a single
-    // CTA's 128-row tile wastes less when M or N is small.
-    if (p.N <= 128) return by_name("umma_128x128x64_s6_ksm");
-    if (p.M <= 128) return by_name("umma_128x256x64_s4_ksm");
-    return by_name("umma_256x256x64_s7_c2_ksm");
-  }
-  return by_name("simt_64x64x16");
+  if (!tma) return by_name("simt_64x64x16");
+  if (p.N <= 128) return by_name("umma_128x128x64_s6_ksm");
+  if (p.M <= 128) return by_name("umma_128x256x64_s4_ksm");
+  // Larger problems, by tile count on the device's SMs:
+  //  - one wave of 128 x 64 tiles and a short K (512^3, 1024^3): the small
+  //    tiles (CTA pairs 1.3-2.1x slower there);
+  //  - fewer than 12 tiles of 256 x 256 and a long K (256^2 and 512^2 x
+  //    65536): split-K on 128 x 128 tiles;
+  //  - otherwise CTA pairs with split-K (1024^2 x 65536, 2048^3 and up).
+  const hw::DeviceLimits* d = hw::current();
+  const long long sms = d && d->sm_count > 0 ? d->sm_count : 148;
+  const long long batch = std::max(1, p.batch);
+  const long long t64 = (long long)ceil_div(p.M, 128) * ceil_div(p.N, 64) * batch;
+  const long long t256 = (long long)ceil_div(p.M, 256) * ceil_div(p.N, 256) * batch;
+  if (t64 <= sms && p.K <= 4096) return by_name("umma_128x64x64_s8_ksm");
+  if (t256 < 12 && p.K > 4096) return by_name("umma_128x128x64_s6_ksm");
+  return by_name("umma_256x256x64_s7_c2_ksm");
 }
 
 Choice choose(std::span<const Winner> table, const gemm::GemmParams& p, const gemm::DeviceCaps& caps,

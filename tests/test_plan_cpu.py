@@ -73,18 +73,31 @@ def test_nearest_m_for_tuned_n_k(M):
 @pytest.mark.parametrize("shape,kernel", [
     ((1, 1000, 3000), "gemv_256x256_ksm"),            # M <= 2: CUDA-core weight stream
     ((2, 1000, 3000), "gemv_256x256_ksm"),
-    ((8, 1000, 3000), "ummav_128x16x64_s6x2"),        # 2 < M <= 16, TMA-addressable
-    ((16, 1000, 3000), "ummav_128x16x64_s6x2"),
+    ((3, 1000, 3000), "ummav_128x16x64_s6x2"),        # 2 < M <= 8, TMA-addressable
+    ((8, 1000, 3000), "ummav_128x16x64_s6x2"),
+    ((9, 1000, 3000), "umma_128x128x64_s6_ksm"),      # 8 < M <= 16: split-K 128 x 128 tiles
+    ((16, 1000, 3000), "umma_128x128x64_s6_ksm"),
     ((8, 1001, 3000), "gemv_128x256_ksm"),            # ldb not a multiple of 8: no TMA
     ((12, 1001, 3000), "gemv_64x256_ksm"),
     ((2000, 120, 3000), "umma_128x128x64_s6_ksm"),    # N <= 128
     ((100, 2000, 3000), "umma_128x256x64_s4_ksm"),    # M <= 128
+    ((600, 600, 600), "umma_128x64x64_s8_ksm"),       # one wave of 128 x 64 tiles, short K
+    ((1000, 1000, 4096), "umma_128x64x64_s8_ksm"),
+    ((384, 384, 40000), "umma_128x128x64_s6_ksm"),    # < 12 tiles of 256 x 256, long K
+    ((1000, 1000, 40000), "umma_256x256x64_s7_c2_ksm"),
     ((2000, 2000, 3000), "umma_256x256x64_s7_c2_ksm"),
+    ((1536, 1536, 1536), "umma_256x256x64_s7_c2_ksm"),
     ((2000, 2001, 3000), "simt_64x64x16"),            # not TMA-addressable
 ])
 def test_built_in_rule_for_untuned_shapes(shape, kernel):
     p = plan(*shape)
     assert p["kind"] == "rule" and p["dispatch"] == kernel, (shape, p)
+
+
+def test_rule_follows_the_sm_count():
+    # 50 tiles of 128 x 64 are one wave on 148 SMs but not on 16.
+    assert plan(600, 600, 600)["dispatch"] == "umma_128x64x64_s8_ksm"
+    assert plan(600, 600, 600, sms=16)["dispatch"] == "umma_256x256x64_s7_c2_ksm"
 
 
 def test_no_winner_rows_off_sm100():
