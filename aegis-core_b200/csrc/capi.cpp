@@ -17,7 +17,7 @@
 #include "aegis/matmul.h"
 #include "capi_error.h"
 #include "common.cuh"
-#include "device.h"
+#include "gpu_target.h"
 #include "kernels.h"
 #include "status.h"
 
@@ -417,21 +417,14 @@ int aegis_plan_simulated_json(int arch, int sm_count, const char* impl, int dtyp
     return fail_arg(fn, "M, N and K must be at most 2^31 - 2^20");
   if (dtype != AEGIS_DTYPE_F16 && dtype != AEGIS_DTYPE_BF16) return fail_arg(fn, "bad dtype");
   if (arch <= 0 || sm_count <= 0 || sm_count > 4096) return fail_arg(fn, "arch and sm_count must be positive");
-  // B200's limits (cudaDeviceProp of the part), with the given arch and SM count.
-  aegis::hw::DeviceLimits sim;
-  sim.name = "simulated";
-  sim.arch = arch;
-  sim.sm_count = sm_count;
-  sim.smem_per_sm = 233472;
-  sim.smem_per_block = 49152;
-  sim.smem_per_block_optin = 232448;
-  sim.regs_per_sm = 65536;
-  sim.regs_per_block = 65536;
-  sim.max_threads_per_sm = 2048;
-  sim.max_threads_per_block = 1024;
-  sim.l2_bytes = size_t(126) << 20;
-  sim.global_mem_bytes = size_t(183359) << 20;
-  const aegis::hw::ScopedSimulation scope(sim);
+  // A B200's per-CTA limits, with the given compute capability and SM count.
+  aegis::gpu::Target model;
+  model.cc = arch;
+  model.sms = sm_count;
+  model.smem_optin = 232448;
+  model.regs_per_cta = 65536;
+  model.threads_per_cta = 1024;
+  const aegis::gpu::PlanOn scope(model);
   static const char dummy[16] alignas(16) = {};
   const aegis::gemm::GemmParams p = aegis::gemm::row_major_params(
       dummy, dummy, const_cast<char*>(dummy), M, N, K,
@@ -440,9 +433,15 @@ int aegis_plan_simulated_json(int arch, int sm_count, const char* impl, int dtyp
   const aegis::detail::Choice c = aegis::detail::choose(aegis::detail::winners_table(), p, caps);
   const char* chosen = c.kernel ? c.kernel->name : "none";
   const char* name = impl ? impl : chosen;
-  if (!aegis::gemm::find(name)) return fail_arg(fn, "no such kernel configuration in the registry");
   aegis::gemm::LaunchPlan pl;
-  if (!aegis::gemm::launch_plan(name, p, &pl)) pl = aegis::gemm::LaunchPlan{};
+  if (impl && std::strcmp(impl, "gemv_noalloc") == 0) {
+    // The plan of aegis_gemv_noalloc (not a registry kernel).
+    if (M > aegis::kNoAllocMaxM || N > aegis::kNoAllocMaxN || !aegis::gemv_noalloc_plan(p, &pl))
+      return fail_arg(fn, "outside the limits of aegis_gemv_noalloc");
+  } else {
+    if (!aegis::gemm::find(name)) return fail_arg(fn, "no such kernel configuration in the registry");
+    if (!aegis::gemm::launch_plan(name, p, &pl)) pl = aegis::gemm::LaunchPlan{};
+  }
   char b[384];
   std::snprintf(b, sizeof b,
                 "{\"impl\":\"%s\",\"splits\":%d,\"k_chunk\":%d,\"tiles\":%lld,\"grid\":%u,\"dispatch\":\"%s\","

@@ -26,10 +26,10 @@
 #include <mutex>
 
 #include "common.cuh"
-#include "device.h"
+#include "gpu_target.h"
 #include "kernels.h"
 #include "ptx.cuh"
-#include "workspace.h"
+#include "scratch.h"
 
 namespace aegis {
 
@@ -303,8 +303,8 @@ GPlan plan_for(int cfg, const GemmParams& p) {
   pl.tiles_n = ceil_div(p.N, c.BN);
   pl.tiles_m = ceil_div(p.M, pl.MT);
   pl.tiles = (long long)pl.tiles_n * pl.tiles_m * p.batch;
-  const hw::DeviceLimits* d = hw::current();
-  const int sms = d ? d->sm_count : 148;
+  const gpu::Target* d = gpu::planning_target();
+  const int sms = d ? d->sms : 148;
   // Split K so that tiles x splits fills one wave (gemv_ctas_per_sm CTAs per
   // SM: ~128 KB of weight loads in flight per SM at MT <= 2), with at least
   // 64 rows a split, and the partials within the workspace cap. A split's A
@@ -428,11 +428,11 @@ cudaError_t gemv_run(int cfg, const GemmParams& p, cudaStream_t stream) {
       const long long tiles = (long long)pl.tiles_n * pl.tiles_m * nb;
       void* cnt = nullptr;
       void* part = nullptr;
-      if (const cudaError_t e = ws::get(stream, size_t(tiles) * sizeof(unsigned), &cnt, ws::Use::SplitKCounters);
+      if (const cudaError_t e = scratch::acquire(stream, size_t(tiles) * sizeof(unsigned), scratch::Kind::Tickets, &cnt);
           e != cudaSuccess)
         return e;
       const size_t pbytes = size_t(tiles) * pl.S * pl.MT * (8 * pl.LPR) * sizeof(float);
-      if (const cudaError_t e = ws::get(stream, pbytes, &part, ws::Use::SplitKPartials); e != cudaSuccess) return e;
+      if (const cudaError_t e = scratch::acquire(stream, pbytes, scratch::Kind::Partials, &part); e != cudaSuccess) return e;
       a.counters = static_cast<unsigned*>(cnt);
       a.partials = static_cast<float*>(part);
     }
@@ -488,7 +488,7 @@ constexpr size_t kNoAllocCounterBytes = size_t(16) << 10;   // 4096 tickets
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocPartialBytes + kNoAllocCounterBytes];
 
 std::mutex g_noalloc_mu;
-unsigned char* g_noalloc_ptr[hw::kMaxCachedDevices] = {};
+unsigned char* g_noalloc_ptr[gpu::kMaxDevices] = {};
 
 // The device address of g_noalloc_scratch on the current device, looked up
 // once per device (with that device current). In host code the symbol itself
@@ -497,7 +497,7 @@ cudaError_t noalloc_scratch(unsigned char** out) {
   *out = nullptr;
   int dev = 0;
   if (const cudaError_t e = cudaGetDevice(&dev); e != cudaSuccess) return e;
-  if (dev < 0 || dev >= hw::kMaxCachedDevices) return cudaErrorInvalidDevice;
+  if (dev < 0 || dev >= gpu::kMaxDevices) return cudaErrorInvalidDevice;
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
   if (!g_noalloc_ptr[dev]) {
     void* p = nullptr;
@@ -508,7 +508,36 @@ cudaError_t noalloc_scratch(unsigned char** out) {
   return cudaSuccess;
 }
 
+// The plan of the CUDA-core GEMV config that ummav_run falls back to for
+// this M (gemv_256 up to M = 4, gemv_128 up to 8, else gemv_64), with fewer,
+// longer splits when its partials would not fit the fixed array. On a B200
+// (148 SMs) the regular plan's partials stay under ~2.4 MiB, so only devices
+// with several hundred SMs take the second branch; aegis_plan_simulated_json
+// reports this plan for a modelled device ("gemv_noalloc"). False when the
+// tickets would not fit.
+bool noalloc_plan(const GemmParams& p, GPlan* out) {
+  GPlan pl = plan_for(p.M <= 4 ? 0 : (p.M <= 8 ? 1 : 2), p);
+  const long long slot_bytes = pl.tiles * pl.MT * (8 * pl.LPR) * (long long)sizeof(float);
+  if ((long long)pl.S * slot_bytes > (long long)kNoAllocPartialBytes) {
+    const long long s_fit = std::max<long long>(1, (long long)kNoAllocPartialBytes / slot_bytes);
+    pl.kc = int(std::min<long long>(ceil_div(ceil_div<long long>(p.K, s_fit), 16ll) * 16, p.K));
+    pl.S = ceil_div(p.K, pl.kc);
+  }
+  *out = pl;
+  return pl.tiles * (long long)sizeof(unsigned) <= (long long)kNoAllocCounterBytes;
+}
+
 }  // namespace
+
+bool gemv_noalloc_plan(const GemmParams& p, gemm::LaunchPlan* out) {
+  GPlan pl{};
+  const bool ok = noalloc_plan(p, &pl);
+  out->splits = pl.S;
+  out->k_chunk = pl.kc;
+  out->tiles = pl.tiles;
+  out->grid = unsigned((long long)pl.tiles_n * pl.S * pl.tiles_m);
+  return ok;
+}
 
 cudaError_t gemv_run_noalloc(const GemmParams& p, cudaStream_t stream, const char** why) {
   *why = "";
@@ -522,17 +551,8 @@ cudaError_t gemv_run_noalloc(const GemmParams& p, cudaStream_t stream, const cha
     return cudaErrorInvalidValue;
   }
   if (p.alpha == 0.f) return scale_c(p, stream);
-  const int cfg = p.M <= 4 ? 0 : (p.M <= 8 ? 1 : 2);  // gemv_256 / gemv_128 / gemv_64 (the dispatcher's rule)
-  GPlan pl = plan_for(cfg, p);
-  const long long slot_bytes = pl.tiles * pl.MT * (8 * pl.LPR) * (long long)sizeof(float);
-  if ((long long)pl.S * slot_bytes > (long long)kNoAllocPartialBytes) {
-    // Fewer, longer splits so the partials fit the fixed array.
-    const long long s_fit = std::max<long long>(1, (long long)kNoAllocPartialBytes / slot_bytes);
-    pl.kc = int(std::min<long long>(ceil_div(ceil_div<long long>(p.K, s_fit), 16ll) * 16, p.K));
-    pl.S = ceil_div(p.K, pl.kc);
-  }
-
-  if (pl.tiles * (long long)sizeof(unsigned) > (long long)kNoAllocCounterBytes) {
+  GPlan pl{};
+  if (!noalloc_plan(p, &pl)) {
     *why = "too many output tiles for the fixed ticket array";
     return cudaErrorInvalidValue;
   }

@@ -51,6 +51,9 @@ size_t ummav_smem_bytes(int cfg);
 inline constexpr int kNoAllocMaxM = 16;
 inline constexpr int kNoAllocMaxN = 65536;
 cudaError_t gemv_run_noalloc(const gemm::GemmParams& p, cudaStream_t stream, const char** why);
+// The plan gemv_run_noalloc would launch on the planning target; false when
+// the problem's tickets do not fit the fixed array.
+bool gemv_noalloc_plan(const gemm::GemmParams& p, gemm::LaunchPlan* out);
 
 // Watchdog self-test kernel: one wait that nothing completes.
 cudaError_t watchdog_selftest(long long limit_ns, cudaStream_t stream, unsigned* bits_out);

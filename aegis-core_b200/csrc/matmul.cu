@@ -11,7 +11,7 @@
 #include "aegis/gemm.h"
 #include "aegis/matmul.h"
 #include "common.cuh"
-#include "device.h"
+#include "gpu_target.h"
 #include "kernels.h"
 
 // One generated table per arch; a missing file means no tuned winners yet.
@@ -39,8 +39,8 @@ cudaError_t fail(cudaError_t e, const std::string& what) {
 }
 
 int current_arch() {
-  const hw::DeviceLimits* d = hw::current();
-  return d ? d->arch : 0;
+  const gpu::Target* d = gpu::planning_target();
+  return d ? d->cc : 0;
 }
 
 const gemm::KernelEntry* find_cached(const detail::Winner& w) {
@@ -87,8 +87,8 @@ const gemm::KernelEntry* rule_for(const gemm::GemmParams& p, const gemm::DeviceC
   //  - fewer than 12 tiles of 256 x 256 and a long K (256^2 and 512^2 x
   //    65536): split-K on 128 x 128 tiles;
   //  - otherwise CTA pairs with split-K (1024^2 x 65536, 2048^3 and up).
-  const hw::DeviceLimits* d = hw::current();
-  const long long sms = d && d->sm_count > 0 ? d->sm_count : 148;
+  const gpu::Target* d = gpu::planning_target();
+  const long long sms = d && d->sms > 0 ? d->sms : 148;
   const long long batch = std::max(1, p.batch);
   const long long t64 = (long long)ceil_div(p.M, 128) * ceil_div(p.N, 64) * batch;
   const long long t256 = (long long)ceil_div(p.M, 256) * ceil_div(p.N, 256) * batch;
@@ -103,21 +103,26 @@ Choice choose(std::span<const Winner> table, const gemm::GemmParams& p, const ge
   const Winner* best = nullptr;
   const gemm::KernelEntry* best_kernel = nullptr;
   double best_dist = INFINITY;
-  for (const Winner& w : table) {
-    if (w.N != p.N || w.K != p.K) continue;
-    const gemm::KernelEntry* e = find_cached(w);
-    std::string reason;
-    if (!e || !gemm::supported(*e, caps, why ? &reason : nullptr)) {
-      ++c.filtered;
-      if (why) *why += std::string(why->empty() ? "" : "; ") + w.impl + ": " + (e ? reason : "not in this build");
-      continue;
+  // Rows of the call's operand type first; the other type's rows only when
+  // (N, K) has no usable row of this one.
+  for (const bool same_type : {true, false}) {
+    for (const Winner& w : table) {
+      if (w.N != p.N || w.K != p.K || (w.dtype == p.dtype) != same_type) continue;
+      const gemm::KernelEntry* e = find_cached(w);
+      std::string reason;
+      if (!e || !gemm::supported(*e, caps, why ? &reason : nullptr)) {
+        ++c.filtered;
+        if (why) *why += std::string(why->empty() ? "" : "; ") + w.impl + ": " + (e ? reason : "not in this build");
+        continue;
+      }
+      const double d = w.M == p.M ? -1.0 : std::abs(std::log2(double(w.M)) - std::log2(double(p.M)));
+      if (!best || d < best_dist || (d == best_dist && w.M > best->M)) {
+        best = &w;
+        best_dist = d;
+        best_kernel = e;
+      }
     }
-    const double d = w.M == p.M ? -1.0 : std::abs(std::log2(double(w.M)) - std::log2(double(p.M)));
-    if (!best || d < best_dist || (d == best_dist && w.M > best->M)) {
-      best = &w;
-      best_dist = d;
-      best_kernel = e;
-    }
+    if (best) break;
   }
   if (best) {
     c.kind = Choice::Kind::Aegis;

@@ -8,7 +8,7 @@
 #include <vector>
 
 #include "aegis/gemm.h"
-#include "device.h"
+#include "gpu_target.h"
 #include "kernels.h"
 
 namespace aegis {
@@ -227,12 +227,12 @@ const KernelEntry* find(std::string_view name) {
 
 DeviceCaps current_caps() {
   DeviceCaps c;
-  const hw::DeviceLimits* d = hw::current();
+  const gpu::Target* d = gpu::planning_target();
   if (!d) return c;
-  c.arch = d->arch;
-  c.smem_per_block_optin = d->smem_per_block_optin;
-  c.regs_per_block = d->regs_per_block;
-  c.max_threads_per_block = d->max_threads_per_block;
+  c.arch = d->cc;
+  c.smem_per_block_optin = d->smem_optin;
+  c.regs_per_block = d->regs_per_cta;
+  c.max_threads_per_block = d->threads_per_cta;
   return c;
 }
 

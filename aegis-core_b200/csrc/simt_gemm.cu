@@ -10,7 +10,7 @@
 #include <algorithm>
 
 #include "common.cuh"
-#include "device.h"
+#include "gpu_target.h"
 #include "kernels.h"
 
 namespace aegis {

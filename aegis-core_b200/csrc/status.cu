@@ -3,13 +3,13 @@
 
 #include <mutex>
 
-#include "device.h"
+#include "gpu_target.h"
 
 namespace aegis::status {
 namespace {
 
 std::mutex g_mu;
-unsigned* g_word[hw::kMaxCachedDevices] = {};
+unsigned* g_word[gpu::kMaxDevices] = {};
 
 }  // namespace
 
@@ -17,7 +17,7 @@ cudaError_t word(unsigned** out) {
   *out = nullptr;
   int dev = 0;
   if (const cudaError_t e = cudaGetDevice(&dev); e != cudaSuccess) return e;
-  if (dev < 0 || dev >= hw::kMaxCachedDevices) return cudaErrorInvalidDevice;
+  if (dev < 0 || dev >= gpu::kMaxDevices) return cudaErrorInvalidDevice;
   std::lock_guard<std::mutex> lock(g_mu);
   if (!g_word[dev]) {
     unsigned* p = nullptr;
@@ -37,7 +37,7 @@ cudaError_t take(unsigned* bits, unsigned* block) {
   *block = 0;
   int dev = 0;
   if (const cudaError_t e = cudaGetDevice(&dev); e != cudaSuccess) return e;
-  if (dev < 0 || dev >= hw::kMaxCachedDevices) return cudaSuccess;
+  if (dev < 0 || dev >= gpu::kMaxDevices) return cudaSuccess;
   unsigned* p = nullptr;
   {
     std::lock_guard<std::mutex> lock(g_mu);

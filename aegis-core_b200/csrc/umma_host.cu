@@ -16,12 +16,12 @@
 #include <mutex>
 
 #include "common.cuh"
-#include "device.h"
+#include "gpu_target.h"
 #include "kernels.h"
 #include "status.h"
 #include "umma_launch.cuh"
 #include "tma_map.h"
-#include "workspace.h"
+#include "scratch.h"
 
 namespace aegis {
 
@@ -119,8 +119,8 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
 
 template <class T>
 cudaError_t launch_reduce(const float* part, int S, const GemmParams& p, cudaStream_t s) {
-  const hw::DeviceLimits* d = hw::physical();
-  const int sms = d ? d->sm_count : 148;
+  const gpu::Target* d = gpu::this_device();
+  const int sms = d ? d->sms : 148;
   const bool vec = p.N % 4 == 0;
   const long long total = (long long)p.batch * p.M * (vec ? p.N / 4 : p.N);
   const int blocks = int(std::max<long long>(1, std::min<long long>((total + 255) / 256, (long long)sms * 8)));
@@ -172,11 +172,11 @@ int group_m_default() {
 // is unavailable (sizing tests on a simulated device).
 int pair_slots(int sms) {
   static std::mutex mu;
-  static int cached[hw::kMaxCachedDevices] = {};
-  const hw::DeviceLimits* d = hw::current();
-  if (!d || d->simulated) return sms;
-  int dev = d->device;
-  if (dev < 0 || dev >= hw::kMaxCachedDevices) return sms;
+  static int cached[gpu::kMaxDevices] = {};
+  const gpu::Target* d = gpu::planning_target();
+  if (!d || d->modelled) return sms;
+  int dev = d->ordinal;
+  if (dev < 0 || dev >= gpu::kMaxDevices) return sms;
   std::lock_guard<std::mutex> lock(mu);
   if (cached[dev] == 0) {
     int n = 0;
@@ -215,9 +215,9 @@ Plan make_plan(int cfg, const GemmParams& p) {
   pl.group_m = group_m_default();
   pl.kb_total = ceil_div(p.K, umma::BK);
   pl.tiles = (long long)p.batch * pl.tiles_m * pl.tiles_n;
-  const hw::DeviceLimits* d = hw::current();
+  const gpu::Target* d = gpu::planning_target();
   // Tile slots: one per SM, or one per resident pair of SMs for cta_group::2.
-  const int sms = d ? (c.CTAS == 2 ? pair_slots(d->sm_count / 2) : d->sm_count) : 0;
+  const int sms = d ? (c.CTAS == 2 ? pair_slots(d->sms / 2) : d->sms) : 0;
   int S = 1;
   if (c.SPLITK && sms > 0 && pl.tiles < sms) {
     // One k-block is BK/16 = 4 MMAs of 128 x BN x 16 (about 128 cycles each at
@@ -283,8 +283,8 @@ static_assert(gemm::UMMA_CONFIGS[kNshardConfig].CTAS == 2 && gemm::UMMA_CONFIGS[
               "the N-sharded path needs the non-split CTA-pair config");
 
 bool device_is_sm100() {
-  const hw::DeviceLimits* d = hw::physical();
-  return d && d->arch == 100;
+  const gpu::Target* d = gpu::this_device();
+  return d && d->cc == 100;
 }
 
 }  // namespace
@@ -306,7 +306,7 @@ cudaError_t umma_run(int cfg, const GemmParams& p, cudaStream_t stream) {
   // Split-K: partials, then the ordered reduction.
   void* part = nullptr;
   const size_t bytes = size_t(pl.splits) * p.batch * size_t(p.M) * p.N * sizeof(float);
-  if (const cudaError_t e = ws::get(stream, bytes, &part, ws::Use::SplitKPartials); e != cudaSuccess) return e;
+  if (const cudaError_t e = scratch::acquire(stream, bytes, scratch::Kind::Partials, &part); e != cudaSuccess) return e;
   a.partials = static_cast<float*>(part);
   k.epi = umma::kEpiPartial;
   if (const cudaError_t e = launch(p, k, maps, a, pl.grid, stream); e != cudaSuccess) return e;

@@ -5,7 +5,7 @@
 #include <cuda.h>
 
 #include "aegis/gemm.h"
-#include "device.h"
+#include "gpu_target.h"
 #include "umma2_kernel.cuh"
 
 namespace aegis::umma {
@@ -21,9 +21,9 @@ template <class T, int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
 cudaError_t launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const Args& a, int grid,
                        cudaStream_t stream) {
   auto* kern = &umma_gemm_kernel<T, BN, STAGES, A_MN, B_MN, EPI>;
-  static hw::PerDevice once;
+  static gpu::SmemOptIn optin;
   constexpr size_t smem = size_t(Layout<BN, STAGES>::ALLOC);
-  if (const cudaError_t e = hw::configure_smem(once, kern, smem); e != cudaSuccess) return e;
+  if (const cudaError_t e = optin.ensure(reinterpret_cast<const void*>(kern), smem); e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(unsigned(grid));
   cfg.blockDim = dim3(kThreads);
@@ -41,9 +41,9 @@ template <class T, int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
 cudaError_t launch_one_pair(const CUtensorMap& ta, const CUtensorMap& tb, const Args& a, int grid,
                             cudaStream_t stream) {
   auto* kern = &umma2_gemm_kernel<T, BN, STAGES, A_MN, B_MN, EPI>;
-  static hw::PerDevice once;
+  static gpu::SmemOptIn optin;
   constexpr size_t smem = size_t(LayoutPair<BN, STAGES>::ALLOC);
-  if (const cudaError_t e = hw::configure_smem(once, kern, smem); e != cudaSuccess) return e;
+  if (const cudaError_t e = optin.ensure(reinterpret_cast<const void*>(kern), smem); e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(unsigned(grid));
   cfg.blockDim = dim3(kThreads);

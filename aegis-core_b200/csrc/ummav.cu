@@ -27,12 +27,12 @@
 #include <algorithm>
 
 #include "common.cuh"
-#include "device.h"
+#include "gpu_target.h"
 #include "kernels.h"
 #include "ptx.cuh"
 #include "status.h"
 #include "tma_map.h"
-#include "workspace.h"
+#include "scratch.h"
 
 namespace aegis {
 namespace ummav {
@@ -367,8 +367,8 @@ Plan make_plan(int cfg, const gemm::GemmParams& p) {
   pl.tiles = ceil_div(p.N, BMN);
   pl.kb = ceil_div(p.K, BK);
   pl.total = (long long)pl.tiles * pl.kb;
-  const hw::DeviceLimits* d = hw::current();
-  const int sms = d ? d->sm_count : 148;
+  const gpu::Target* d = gpu::planning_target();
+  const int sms = d ? d->sms : 148;
   pl.grid = int(std::max<long long>(1, std::min<long long>(pl.total, (long long)sms * c.CTAS_PER_SM)));
   const long long per = pl.total / pl.grid;  // smallest range
   pl.maxseg = int(std::min<long long>(pl.grid, (pl.kb + std::max<long long>(1, per) - 1) / std::max<long long>(1, per) + 1));
@@ -378,9 +378,9 @@ Plan make_plan(int cfg, const gemm::GemmParams& p) {
 template <class T, int STAGES>
 cudaError_t launch_s(const CUtensorMap& ta, const CUtensorMap& tb, const Args& a, int grid, cudaStream_t s) {
   auto* kern = &ummav_kernel<T, STAGES>;
-  static hw::PerDevice once;
+  static gpu::SmemOptIn optin;
   constexpr size_t smem = size_t(Layout<STAGES>::ALLOC);
-  if (const cudaError_t e = hw::configure_smem(once, kern, smem); e != cudaSuccess) return e;
+  if (const cudaError_t e = optin.ensure(reinterpret_cast<const void*>(kern), smem); e != cudaSuccess) return e;
   // Programmatic dependent launch: this grid's prologue (barrier set-up, TMEM
   // allocation, descriptor prefetch) may overlap the previous grid's tail on
   // the stream; the kernel waits (griddepcontrol.wait) before touching memory.
@@ -414,8 +414,8 @@ bool ummav_takes(const gemm::GemmParams& p) {
 }
 
 bool ummav_applicable(const gemm::GemmParams& p) {
-  const hw::DeviceLimits* d = hw::physical();
-  return d && d->arch == 100 && ummav_takes(p);
+  const gpu::Target* d = gpu::this_device();
+  return d && d->cc == 100 && ummav_takes(p);
 }
 
 cudaError_t ummav_run(int cfg, const gemm::GemmParams& p, cudaStream_t stream) {
@@ -449,11 +449,11 @@ cudaError_t ummav_run(int cfg, const gemm::GemmParams& p, cudaStream_t stream) {
   if (pl.maxseg > 1) {
     void* cnt = nullptr;
     void* part = nullptr;
-    if (const cudaError_t e = ws::get(stream, size_t(pl.tiles) * 4 * sizeof(unsigned), &cnt, ws::Use::SplitKCounters);
+    if (const cudaError_t e = scratch::acquire(stream, size_t(pl.tiles) * 4 * sizeof(unsigned), scratch::Kind::Tickets, &cnt);
         e != cudaSuccess)
       return e;
     const size_t pbytes = size_t(pl.tiles) * pl.maxseg * ummav::MPAD * ummav::BMN * sizeof(float);
-    if (const cudaError_t e = ws::get(stream, pbytes, &part, ws::Use::SplitKPartials); e != cudaSuccess) return e;
+    if (const cudaError_t e = scratch::acquire(stream, pbytes, scratch::Kind::Partials, &part); e != cudaSuccess) return e;
     a.counters = static_cast<unsigned*>(cnt);
     a.partials = static_cast<float*>(part);
   }

@@ -250,24 +250,24 @@ def pick(con: sqlite3.Connection, arch: int) -> int:
 
 
 def header_text(con: sqlite3.Connection, arch: int, generated: str) -> tuple[str, int]:
-    """The winners header: one row per shape (bf16 preferred when a shape was
-    tuned in both 16-bit types; the dispatch is shape-keyed)."""
+    """The winners header: one row per (shape, operand type) tuned; dispatch
+    prefers the rows of the call's type."""
     rows = con.execute(
         "SELECT w.shape_bucket, w.dtype, k.impl, w.pct_of_cublas, w.tied, w.tie_set, w.pick_reason, w.tie_method, "
         "w.ratio_ci_lo, w.ratio_ci_hi, w.cublas_ratio_ci_lo, w.cublas_ratio_ci_hi, w.median_us FROM winners w "
         "JOIN kernels k USING (kernel_id) WHERE w.sm_arch = ? AND w.op = 'gemm'", (arch,)).fetchall()
-    by_shape: dict[tuple[int, int, int], tuple] = {}
+    by_shape: dict[tuple[int, int, int, str], tuple] = {}
     for r in rows:
         m, n, k = (int(x) for x in r[0].split("x"))
-        if (m, n, k) not in by_shape or r[1] == "bf16":
-            by_shape[(m, n, k)] = r
+        by_shape[(m, n, k, r[1])] = r
     name = f"sm{arch}a" if arch == 100 else f"sm{arch}"
     out = [
         f"// Generated by aegis_perf.py emit-header, {generated}.",
         "// Do not edit. Regenerate on the device after tuning (aegis_tune -> aegis_perf.py ingest, pick, emit-header).",
         f"// Tuned GEMM winners for {name}, read by aegis::matmul (csrc/matmul.cu).",
         "// Row: M, N, K, tuned impl, dispatch (always Aegis: no vendor-library dispatch), kernel % of cuBLAS",
-        "// (median ratio of the tuning run), paired 95% CI of cuBLAS time / winner time (0, 0: none).",
+        "// (median ratio of the tuning run), paired 95% CI of cuBLAS time / winner time (0, 0: none),",
+        "// operand type the row was tuned on.",
         "// \"[tie test ...]\" in a comment: the paired CI of runner-up / winner time.",
         "#pragma once",
         '#include "aegis/matmul.h"',
@@ -278,7 +278,7 @@ def header_text(con: sqlite3.Connection, arch: int, generated: str) -> tuple[str
         return "\n".join(out) + "\n", 0
     define = "AEGIS_WINNERS_SM100" if arch == 100 else f"AEGIS_WINNERS_SM{arch}"
     out += [f"#define {define} 1", f"inline constexpr aegis::detail::Winner kWinners_{name}[] = {{"]
-    for (m, n, k), r in sorted(by_shape.items(), key=lambda kv: (kv[0][1], kv[0][2], kv[0][0])):
+    for (m, n, k, _), r in sorted(by_shape.items(), key=lambda kv: (kv[0][1], kv[0][2], kv[0][0], kv[0][3])):
         (_, dtype, impl, pct, tied, tie_set, reason, method, lo, hi, clo, chi, med) = r
         note = [f"{dtype}, {med:.2f} us"]
         if clo is not None:
@@ -293,7 +293,8 @@ def header_text(con: sqlite3.Connection, arch: int, generated: str) -> tuple[str
         elif reason and reason != "fastest":
             note.append(reason)
         out.append(f'    {{{m}, {n}, {k}, "{impl}", aegis::detail::Dispatch::Aegis, {pct:.1f}, {clo or 0:.4f}, '
-                   f'{chi or 0:.4f}}},  // ' + "; ".join(note))
+                   f'{chi or 0:.4f}, aegis::gemm::DType::{"BF16" if dtype == "bf16" else "F16"}}},  // '
+                   + "; ".join(note))
     out.append("};")
     return "\n".join(out) + "\n", len(by_shape)
 

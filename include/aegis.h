@@ -261,7 +261,8 @@ AEGIS_API int aegis_gemm_plan_json(aegis_context* ctx, const char* impl, int dty
  * SMs and B200's other limits. JSON as aegis_gemm_plan_json plus
  * "kind":"winner" (a tuned winners row chose it) or "rule" (the built-in
  * rule), and "dispatch" (the chosen kernel; `impl` only replaces the kernel
- * whose plan is reported). Runs nothing on any GPU; for planning tools and
+ * whose plan is reported; impl "gemv_noalloc" reports the plan of
+ * aegis_gemv_noalloc below). Runs nothing on any GPU; for planning tools and
  * tests of the dispatch rules on machines without one. No reference
  * counterpart (the reference tests dispatch on its device only,
  * tests/test_matmul.cu). */

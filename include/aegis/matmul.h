@@ -4,7 +4,10 @@
 // matmul.h:8-123) with B200 rules:
 //
 // Selection, against the winners compiled in for the device's arch
-// (include/aegis/winners/sm_100a.h, written by the tuner's emit-header step):
+// (include/aegis/winners/sm_100a.h, written by the tuner's emit-header step),
+// among the rows tuned on the call's operand type (f16 or bf16); when (N, K)
+// has none of that type, the other 16-bit type's rows (the same kernel
+// templates serve both types):
 //   1. exact (M, N, K) match;
 //   2. else the winner with the same N and K whose M is nearest in log2 (ties
 //      go to the larger M);
@@ -41,6 +44,7 @@ struct Winner {
   Dispatch dispatch = Dispatch::Aegis;
   double pct_of_cublas = 0;       // kernel % of cuBLAS (paired median; 0 = not measured)
   double ci_lo = 0, ci_hi = 0;    // paired CI of cuBLAS time / kernel time (0 = none)
+  gemm::DType dtype = gemm::DType::F16;  // operand type the row was tuned on
 };
 
 struct Choice {

@@ -2,8 +2,8 @@
 
 Covers the reference's correctness cases (tests/test_tma.cu, test_matmul.cu,
 bench_gemm --check shapes in its CMakeLists.txt:202-212): every registry
-kernel on the golden fixtures (outputs of the reference's own oracle), BASELINE
-config 1 (512^3 f16, seed 0) and config 2 (the square sweep, f16 and bf16,
+kernel on the golden fixtures (outputs of the reference's own oracle), the
+512^3 f16 workload (seed 0) and the square sweep (1024^3-8192^3, f16 and bf16,
 sampled rows against the oracle plus the full matrix against cuBLAS), every
 layout pair on the tcgen05 path, alpha/beta/batch, NaN/Inf, alpha == 0,
 empty sizes, and misaligned operands (general kernel)."""
@@ -95,7 +95,7 @@ def _sample_rows(M):
 @pytest.mark.parametrize("dtype", ["f16", "bf16"])
 @pytest.mark.parametrize("n", [1024, 2048, 4096, 8192])
 def test_square_sweep_config2(cuda, dtype, n):
-    """C = A*B, M = N = K = n, uniform[-1, 1] from seed 0.
+    """Square sweep: C = A*B, M = N = K = n, uniform[-1, 1] from seed 0.
     Sampled rows against the FP64 oracle, the whole matrix against cuBLAS."""
     torch = cuda
     d = op.make_desc(n, n, n, dtype=dtype)
@@ -180,13 +180,14 @@ def test_watchdog_selftest_and_context_reuse(cuda):
 
 
 def _winner_rows():
-    """(M, N, K, impl) of every row of the committed winners header."""
+    """(M, N, K, impl) of every f16 row of the committed winners header (the
+    type aegis_gemm_choice asks about)."""
     import re
     path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "aegis", "winners",
                         "sm_100a.h")
     if not os.path.exists(path):
         return []
-    pat = re.compile(r'^\s*\{(\d+), (\d+), (\d+), "([^"]+)", aegis::detail::Dispatch::Aegis')
+    pat = re.compile(r'^\s*\{(\d+), (\d+), (\d+), "([^"]+)", aegis::detail::Dispatch::Aegis.*DType::F16\}')
     return [(int(m[1]), int(m[2]), int(m[3]), m[4]) for m in map(pat.match, open(path)) if m]
 
 

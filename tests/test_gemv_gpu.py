@@ -1,4 +1,4 @@
-"""Decode GEMV parity: M in {1, 4, 16}, activations
+"""Decode GEMV parity (the decode workload): M in {1, 4, 16}, activations
 ~N(0, 1), f16 weights ~N(0, 0.02) of K x N in {4096x4096, 4096x14336,
 14336x4096}, std::mt19937 + std::normal_distribution<float> on the host;
 every gemv configuration and the dispatcher, against the FP64 oracle with

@@ -1,7 +1,7 @@
 """The oracle (oracle/oracle.c) pinned against the reference's own outputs.
 
 - Known answers of the reference's aegis::bench::cpu_reference on BASELINE
-  config 1 (M = N = K = 512, std::mt19937(0), uniform[-1, 1], A then B).
+  512^3 f16 workload (M = N = K = 512, std::mt19937(0), uniform[-1, 1], A then B).
 - Golden fixtures written by tests/golden/make_golden.py from the reference's
   own oracle (compiled from its source into oracle/_ref): layouts, padded
   leading dimensions, alpha/beta, strided batch, NaN/Inf, alpha == 0.

@@ -24,28 +24,41 @@ HEADER = os.path.join(ROOT, "include", "aegis", "winners", "sm_100a.h")
 BF16 = ac.DTYPE_BF16
 
 
-def winner_rows():
+def winner_rows(dtype="bf16"):
+    """(M, N, K, impl) of the header's rows tuned on `dtype`."""
     rows = []
     for line in open(HEADER):
-        m = re.match(r'\s*\{(\d+), (\d+), (\d+), "([^"]+)"', line)
-        if m:
+        m = re.match(r'\s*\{(\d+), (\d+), (\d+), "([^"]+)".*DType::(BF16|F16)\}', line)
+        if m and m.group(5).lower() == dtype:
             rows.append((int(m.group(1)), int(m.group(2)), int(m.group(3)), m.group(4)))
     return rows
 
 
-def plan(M, N, K, impl=None, sms=148, arch=100):
-    return ac.plan_simulated(M, N, K, impl=impl, dtype=BF16, arch=arch, sm_count=sms)
+def plan(M, N, K, impl=None, sms=148, arch=100, dtype=BF16):
+    return ac.plan_simulated(M, N, K, impl=impl, dtype=dtype, arch=arch, sm_count=sms)
 
 
 def test_header_has_rows():
-    assert len(winner_rows()) >= 17
+    assert len(winner_rows("bf16")) >= 17 and len(winner_rows("f16")) >= 17
 
 
-@pytest.mark.parametrize("row", winner_rows(), ids=lambda r: f"{r[0]}x{r[1]}x{r[2]}")
-def test_winner_rows_are_chosen_for_their_shape(row):
-    M, N, K, impl = row
-    p = plan(M, N, K)
-    assert p["kind"] == "winner" and p["dispatch"] == impl and p["impl"] == impl, p
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+def test_winner_rows_are_chosen_for_their_shape_and_type(dtype):
+    code = BF16 if dtype == "bf16" else ac.DTYPE_F16
+    for M, N, K, impl in winner_rows(dtype):
+        p = plan(M, N, K, dtype=code)
+        assert p["kind"] == "winner" and p["dispatch"] == impl and p["impl"] == impl, (dtype, M, N, K, p)
+
+
+def test_rows_of_the_other_type_serve_an_untuned_type():
+    """(N, K) tuned in only one type: a call of the other type takes that
+    type's rows (nearest M), not the built-in rule. Checked on every bf16 (N, K)
+    with no f16 row, else vacuously."""
+    f16_nk = {(n, k) for (_, n, k, _) in winner_rows("f16")}
+    for (M, N, K, impl) in winner_rows("bf16"):
+        if (N, K) not in f16_nk:
+            p = plan(M, N, K, dtype=ac.DTYPE_F16)
+            assert p["kind"] == "winner" and p["dispatch"] == impl
 
 
 def nearest(rows, M, N, K):
@@ -212,3 +225,62 @@ def test_arguments_are_checked():
         ac.plan_simulated(8, 8, 8, sm_count=0)
     with pytest.raises(ac.AegisError):
         ac.plan_simulated(8, 8, 8, dtype=7)
+
+
+NOALLOC_PARTIAL_BYTES = 4 << 20  # the fixed partials array of aegis_gemv_noalloc
+
+
+def _noalloc_cfg(M):
+    """(impl, BN, MT) of the CUDA-core GEMV config aegis_gemv_noalloc runs for M."""
+    impl, bn = ("gemv_256x256_ksm", 256) if M <= 4 else (("gemv_128x256_ksm", 128) if M <= 8 else
+                                                         ("gemv_64x256_ksm", 64))
+    mt = 1
+    while mt < M and mt < 16 and mt < 1024 // bn:
+        mt *= 2
+    return impl, bn, mt
+
+
+@pytest.mark.parametrize("sms", [148, 592, 2048, 4096])
+@pytest.mark.parametrize("M", [1, 4, 8, 16])
+@pytest.mark.parametrize("N,K", [(4096, 4096), (14336, 4096), (4096, 14336), (65536, 65536), (512, 131072)])
+def test_noalloc_plan_fits_the_fixed_array(sms, M, N, K):
+    """The allocation-free GEMV keeps the regular plan while its FP32 partials
+    fit the 4 MiB array, and otherwise re-splits K into fewer, longer chunks
+    that still cover K with no empty split. On 148 SMs the regular plan always
+    fits; the many-SM devices force the re-split branch."""
+    impl, bn, mt = _noalloc_cfg(M)
+    got = plan(M, N, K, impl="gemv_noalloc", sms=sms)
+    reg = plan(M, N, K, impl=impl, sms=sms)
+    assert got["tiles"] == reg["tiles"]
+    slot = got["tiles"] * mt * bn * 4  # one split's partials: tiles x MT x BN floats
+    S, kc = got["splits"], got["k_chunk"]
+    assert kc % 16 == 0 or kc == K
+    assert S == math.ceil(K / kc) and (S - 1) * kc < K <= S * kc
+    if S > 1:
+        assert S * slot <= NOALLOC_PARTIAL_BYTES
+    if reg["splits"] * slot <= NOALLOC_PARTIAL_BYTES:
+        assert (S, kc) == (reg["splits"], reg["k_chunk"])
+    else:
+        assert S < reg["splits"]
+
+
+def test_noalloc_plan_re_splits_on_a_many_sm_device():
+    """At least one shape takes the fewer-splits branch on a 4096-SM device,
+    and none does on a B200's 148 SMs."""
+    shapes = [(M, N, K) for M in (1, 4, 8, 16) for N, K in ((4096, 4096), (14336, 4096), (4096, 14336))]
+    def re_split(sms):
+        out = []
+        for M, N, K in shapes:
+            impl = _noalloc_cfg(M)[0]
+            if plan(M, N, K, impl="gemv_noalloc", sms=sms)["splits"] != plan(M, N, K, impl=impl, sms=sms)["splits"]:
+                out.append((M, N, K))
+        return out
+    assert re_split(148) == []
+    assert len(re_split(4096)) > 0
+
+
+def test_noalloc_plan_refuses_out_of_limit_shapes():
+    with pytest.raises(ac.AegisError):
+        plan(17, 4096, 4096, impl="gemv_noalloc")
+    with pytest.raises(ac.AegisError):
+        plan(1, 65537, 4096, impl="gemv_noalloc")

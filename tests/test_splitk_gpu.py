@@ -1,4 +1,5 @@
-"""Deterministic split-K on the GPU (BASELINE config 4 and the reference's
+"""Deterministic split-K on the GPU (the tall-K workload, M = N in {256, 512,
+1024} x K = 65536, and the reference's
 tests/test_splitk.cu pattern): tall-K shapes split by the SM count, 10 runs
 bitwise identical, within tolerance of the FP64 oracle; odd split counts and
 K tails; general layouts with beta; the first call for a stream inside CUDA

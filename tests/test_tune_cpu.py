@@ -127,18 +127,19 @@ def test_header_rows_sorted_and_compile(tmp_path, db):
         meas("tune-1", "cublas", 1, 14336, 4096, 20.0), meas("tune-1", "gemv_256x256_ksm", 1, 14336, 4096, 23.0),
         meas("tune-1", "umma_128x128x64_s6_ksm", 1, 14336, 4096, 40.0),
         paired("tune-1", "gemv_256x256_ksm", "cublas", "cublas", 1, 4096, 4096, 1.21, 1.26),
-        # The same shape tuned in f16 too: the header keeps the bf16 row.
+        # The same shape tuned in f16 too: one row per operand type.
         meas("tune-1", "umma_128x256x64_s4", 4096, 4096, 4096, 120.0, dtype="f16"),
     ]
     ap.ingest(db, write(tmp_path, "r.jsonl", rows))
     ap.pick(db, 100)
     text, n = ap.header_text(db, 100, "test")
-    assert n == 3
+    assert n == 4
     body = [ln for ln in text.splitlines() if ln.startswith("    {")]
-    # Sorted by (N, K, M).
+    # Sorted by (N, K, M, type).
     assert [ln.split(",")[:3] for ln in body] == [["    {1", " 4096", " 4096"], ["    {4096", " 4096", " 4096"],
-                                                  ["    {1", " 14336", " 4096"]]
-    assert '"umma_256x256x64_s7_c2"' in body[1] and "bf16" in body[1]
+                                                  ["    {4096", " 4096", " 4096"], ["    {1", " 14336", " 4096"]]
+    assert '"umma_256x256x64_s7_c2"' in body[1] and "DType::BF16}" in body[1]
+    assert '"umma_128x256x64_s4"' in body[2] and "DType::F16}" in body[2]
     assert "123.8% of cuBLAS (paired CI 121.0-126.0%)" in body[0]  # 13.0 / 10.5 us
     assert "#define AEGIS_WINNERS_SM100 1" in text and "kWinners_sm100a[]" in text
     hdr = tmp_path / "inc" / "aegis" / "winners"
@@ -146,8 +147,9 @@ def test_header_rows_sorted_and_compile(tmp_path, db):
     (hdr / "sm_100a.h").write_text(text)
     tu = tmp_path / "tu.cpp"
     tu.write_text('#include "aegis/winners/sm_100a.h"\n'
-                  "static_assert(sizeof(kWinners_sm100a) / sizeof(kWinners_sm100a[0]) == 3);\n"
-                  "static_assert(kWinners_sm100a[0].M == 1 && kWinners_sm100a[2].N == 14336);\n"
+                  "static_assert(sizeof(kWinners_sm100a) / sizeof(kWinners_sm100a[0]) == 4);\n"
+                  "static_assert(kWinners_sm100a[0].M == 1 && kWinners_sm100a[3].N == 14336);\n"
+                  "static_assert(kWinners_sm100a[2].dtype == aegis::gemm::DType::F16);\n"
                   "int main() { return 0; }\n")
     cxx = shutil.which("g++")
     if cxx is None:

@@ -10,6 +10,10 @@ inside the library. These tests call it through the C ABI and check that its
 output matches the regular entry point's (aegis_gemm_*_ex) within the
 tolerance the other tests use, on two calls in a row (the second call finds
 the array as the first one left it), and that the calls allocate nothing.
+The one planning step that differs from the regular entry point (fewer,
+longer K splits when the partials would overflow the array) is reached only
+on devices with several hundred SMs; tests/test_plan_cpu.py checks it on a
+modelled device.
 This file is collected last on purpose; it passes alone or after the rest.
 """
 import numpy as np
