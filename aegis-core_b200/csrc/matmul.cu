@@ -153,8 +153,13 @@ cudaError_t matmul(const gemm::GemmParams& p, cudaStream_t stream) {
   return e == cudaSuccess ? e : fail(e, std::string("launch ") + c.kernel->name);
 }
 
-cudaError_t matmul(const void* A, const void* B, void* C, int M, int N, int K, cudaStream_t stream) {
-  return matmul(gemm::row_major_params(A, B, C, M, N, K), stream);
+cudaError_t matmul(const __half* A, const __half* B, __half* C, int M, int N, int K, cudaStream_t stream) {
+  return matmul(gemm::row_major_params(A, B, C, M, N, K, gemm::DType::F16), stream);
+}
+
+cudaError_t matmul(const __nv_bfloat16* A, const __nv_bfloat16* B, __nv_bfloat16* C, int M, int N, int K,
+                   cudaStream_t stream) {
+  return matmul(gemm::row_major_params(A, B, C, M, N, K, gemm::DType::BF16), stream);
 }
 
 const char* matmul_last_error() { return t_last_error.c_str(); }

@@ -10,8 +10,11 @@ The subset of the reference's `aegis-perf` crate (rust/aegis-perf/src/
 {db.rs,tune.rs,schema.sql}) that turns tuner runs into dispatch:
   - schema: the runs / kernels / measurements / paired / winners /
     schema_version tables of schema.sql:2-108, with the columns this library
-    produces (no cuBLASLt algorithm columns: nothing here dispatches to a
-    vendor library);
+    produces: the winners' percent of cuBLAS and of cublaslt_best and their
+    paired CIs (schema.sql:63-68), but no cuBLASLt algorithm columns, since
+    nothing here dispatches to a vendor library;
+  - the baselines ("cublas", "cublaslt_best") are measured beside the
+    kernels and never win;
   - kernel_id = sha1("op|impl|config"), as db.rs keys kernels;
   - winner per (arch, op, dtype, shape): the fastest cold median of the
     shape's latest run. The paired tie test decides ties (tune.rs): the
@@ -33,7 +36,7 @@ import os
 import sqlite3
 import sys
 
-SCHEMA_VERSION = 1
+SCHEMA_VERSION = 2
 
 SCHEMA = """
 CREATE TABLE IF NOT EXISTS runs (
@@ -108,6 +111,9 @@ CREATE TABLE IF NOT EXISTS winners (
   ratio_ci_hi REAL,
   cublas_ratio_ci_lo REAL,
   cublas_ratio_ci_hi REAL,
+  pct_of_cublaslt_best REAL,
+  lt_ratio_ci_lo REAL,
+  lt_ratio_ci_hi REAL,
   PRIMARY KEY (sm_arch, op, dtype, shape_bucket)
 );
 CREATE TABLE IF NOT EXISTS schema_version (
@@ -200,8 +206,9 @@ def pick(con: sqlite3.Connection, arch: int) -> int:
             "SELECT k.impl, m.kernel_id, m.median_us, m.p10_us, m.p90_us FROM measurements m JOIN kernels k "
             "USING (kernel_id) WHERE m.run_id = ? AND k.op = ? AND m.dtype = ? AND m.m = ? AND m.n = ? AND m.k = ? "
             "AND m.pass = 1 ORDER BY m.median_us", (run, op, dtype, mm, nn, kk)).fetchall()
-        ours = [x for x in meas if x[0] != "cublas"]
+        ours = [x for x in meas if not x[0].startswith("cublas")]
         base = next((x for x in meas if x[0] == "cublas"), None)
+        lt = next((x for x in meas if x[0] == "cublaslt_best"), None)
         if not ours:
             continue
         fastest, runner = ours[0], (ours[1] if len(ours) > 1 else None)
@@ -237,13 +244,18 @@ def pick(con: sqlite3.Connection, arch: int) -> int:
             else:
                 reason = "fastest (tie)"
         pct = base[2] / choice[2] * 100.0 if base else 0.0
+        pct_lt = lt[2] / choice[2] * 100.0 if lt else None
         cb = paired_row("cublas", fastest[0])
+        lb = paired_row("cublaslt_best", fastest[0])
+        mine = choice is fastest
         con.execute(
             "INSERT OR REPLACE INTO winners (sm_arch, op, dtype, shape_bucket, kernel_id, run_id, median_us, "
             "pct_of_cublas, tied, tie_set, pick_reason, protocol_version, tie_method, ratio_ci_lo, ratio_ci_hi, "
-            "cublas_ratio_ci_lo, cublas_ratio_ci_hi) VALUES (?,?,?,?,?,?,?,?,?,?,?,2,?,?,?,?,?)",
+            "cublas_ratio_ci_lo, cublas_ratio_ci_hi, pct_of_cublaslt_best, lt_ratio_ci_lo, lt_ratio_ci_hi) "
+            "VALUES (?,?,?,?,?,?,?,?,?,?,?,2,?,?,?,?,?,?,?,?)",
             (arch, op, dtype, bucket, choice[1], run, choice[2], pct, tied, json.dumps(tie_set), reason, method,
-             ci[0], ci[1], cb[0] if cb and choice is fastest else None, cb[1] if cb and choice is fastest else None))
+             ci[0], ci[1], cb[0] if cb and mine else None, cb[1] if cb and mine else None, pct_lt,
+             lb[0] if lb and mine else None, lb[1] if lb and mine else None))
         written += 1
     con.commit()
     return written
@@ -254,7 +266,8 @@ def header_text(con: sqlite3.Connection, arch: int, generated: str) -> tuple[str
     prefers the rows of the call's type."""
     rows = con.execute(
         "SELECT w.shape_bucket, w.dtype, k.impl, w.pct_of_cublas, w.tied, w.tie_set, w.pick_reason, w.tie_method, "
-        "w.ratio_ci_lo, w.ratio_ci_hi, w.cublas_ratio_ci_lo, w.cublas_ratio_ci_hi, w.median_us FROM winners w "
+        "w.ratio_ci_lo, w.ratio_ci_hi, w.cublas_ratio_ci_lo, w.cublas_ratio_ci_hi, w.median_us, "
+        "w.pct_of_cublaslt_best FROM winners w "
         "JOIN kernels k USING (kernel_id) WHERE w.sm_arch = ? AND w.op = 'gemm'", (arch,)).fetchall()
     by_shape: dict[tuple[int, int, int, str], tuple] = {}
     for r in rows:
@@ -279,12 +292,14 @@ def header_text(con: sqlite3.Connection, arch: int, generated: str) -> tuple[str
     define = "AEGIS_WINNERS_SM100" if arch == 100 else f"AEGIS_WINNERS_SM{arch}"
     out += [f"#define {define} 1", f"inline constexpr aegis::detail::Winner kWinners_{name}[] = {{"]
     for (m, n, k, _), r in sorted(by_shape.items(), key=lambda kv: (kv[0][1], kv[0][2], kv[0][0], kv[0][3])):
-        (_, dtype, impl, pct, tied, tie_set, reason, method, lo, hi, clo, chi, med) = r
+        (_, dtype, impl, pct, tied, tie_set, reason, method, lo, hi, clo, chi, med, pct_lt) = r
         note = [f"{dtype}, {med:.2f} us"]
         if clo is not None:
             note.append(f"{pct:.1f}% of cuBLAS (paired CI {clo * 100:.1f}-{chi * 100:.1f}%)")
         else:
             note.append(f"{pct:.1f}% of cuBLAS (unpaired)")
+        if pct_lt is not None:
+            note.append(f"{pct_lt:.1f}% of cublaslt_best")
         if method in ("paired", "paired_swap") and lo is not None:
             note.append(f"[tie test runner-up / winner {lo:.3f}-{hi:.3f}]")
         if tied:
@@ -303,18 +318,21 @@ def table(path: str) -> str:
     rows = [json.loads(ln) for ln in open(path) if ln.strip().startswith("{")]
     meas = [r for r in rows if r.get("kind") == "measurement"]
     shapes = sorted({(r["m"], r["n"], r["k"], r["dtype"]) for r in meas})
-    lines = [f"{'shape':>22} {'dtype':>5} {'winner':>28} {'us':>9} {'TFLOP/s':>8} {'GB/s(w)':>8} {'% cuBLAS':>8}"]
+    lines = [f"{'shape':>22} {'dtype':>5} {'winner':>28} {'us':>9} {'TFLOP/s':>8} {'GB/s(w)':>8} {'% cuBLAS':>8} "
+             f"{'% Lt best':>9}"]
     for m, n, k, d in shapes:
         rs = sorted((r for r in meas if (r["m"], r["n"], r["k"], r["dtype"]) == (m, n, k, d)),
                     key=lambda r: r["median_us"])
-        ours = [r for r in rs if r["impl"] != "cublas"]
+        ours = [r for r in rs if not r["impl"].startswith("cublas")]
         cb = next((r for r in rs if r["impl"] == "cublas"), None)
+        lt = next((r for r in rs if r["impl"] == "cublaslt_best"), None)
         if not ours:
             continue
         w = ours[0]
         pct = cb["median_us"] / w["median_us"] * 100 if cb else 0.0
+        pct_lt = f"{lt['median_us'] / w['median_us'] * 100:9.1f}" if lt else f"{'-':>9}"
         lines.append(f"{f'{m}x{n}x{k}':>22} {d:>5} {w['impl']:>28} {w['median_us']:9.2f} {w['tflops']:8.1f} "
-                     f"{w.get('weights_gbps', 0):8.0f} {pct:8.1f}")
+                     f"{w.get('weights_gbps', 0):8.0f} {pct:8.1f} {pct_lt}")
     return "\n".join(lines) + "\n"
 
 

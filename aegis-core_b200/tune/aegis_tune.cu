@@ -17,12 +17,18 @@
 //     configuration that errors or fails is listed on stderr and not timed),
 //     then `reps` timed windows, each a CUDA graph of batch_n launches sized
 //     to >= window-ms, timed with events on the stream;
-//   - paired tie test: the fastest configuration against the runner-up and
-//     against cuBLAS over `pairs` alternating windows (a, b, a, b, ...); the
+//   - cublaslt_best (reference src/bench/harness.cu:1006-1031): the cuBLASLt
+//     heuristic's top 8 algorithms for the shape (32 MiB workspace; split-K
+//     algorithms with reduced-precision partials dropped, tune/lt_best.h),
+//     each checked and timed like the configurations; the fastest is
+//     reported as impl "cublaslt_best" with its algorithm in "config";
+//   - paired tie test: the fastest configuration against the runner-up,
+//     against cuBLAS and against cublaslt_best over `pairs` alternating
+//     windows (a, b, a, b, ...); the
 //     95% percentile-bootstrap CI (2000 resamples, seeded) of the median of
 //     the per-pair ratios b / a.
 // stdout: JSON lines. {"kind":"run",...} once; {"kind":"measurement",...} per
-// timed configuration (the baseline has impl "cublas"); {"kind":"paired",...}
+// timed configuration (the baselines have impl "cublas" and "cublaslt_best"); {"kind":"paired",...}
 // per tie test. aegis_perf.py ingests them into the perf DB and emits
 // include/aegis/winners/sm_100a.h.
 #include <cublas_v2.h>
@@ -38,12 +44,14 @@
 #include <cstring>
 #include <ctime>
 #include <fstream>
+#include <memory>
 #include <random>
 #include <sstream>
 #include <string>
 #include <vector>
 
 #include "aegis.h"
+#include "lt_best.h"
 
 namespace {
 
@@ -267,6 +275,7 @@ class Tuner {
     CK(cudaEventCreate(&e0_));
     CK(cudaEventCreate(&e1_));
     CK(cudaMalloc(&maxdiff_, sizeof(unsigned)));
+    CK(cudaMalloc(&lt_ws_, kLtWorkspace));
     CK(cudaGetDeviceProperties(&prop_, 0));
   }
   ~Tuner() {
@@ -339,6 +348,9 @@ class Tuner {
       return cublasGemmEx(blas_, CUBLAS_OP_N, CUBLAS_OP_N, p.N, p.M, p.K, &one, p.B[i], t, p.N, p.A[i], t, p.K, &zero,
                           C, t, p.N, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT) == CUBLAS_STATUS_SUCCESS;
     }
+    if (impl.rfind("cublaslt#", 0) == 0)  // candidate n of the shape's cuBLASLt sweep
+      return lt_ && lt_->run(std::atoi(impl.c_str() + 9), p.A[i], p.B[i], C, lt_ws_, kLtWorkspace, stream_) ==
+                        CUBLAS_STATUS_SUCCESS;
     return aegis_gemm_impl(ctx_, impl.c_str(), a_.dtype, AEGIS_ROW_MAJOR, AEGIS_ROW_MAJOR, p.M, p.N, p.K, 1.f, p.A[i],
                            p.K, 0, p.B[i], p.N, 0, 0.f, C, p.N, 0, 1) == AEGIS_OK;
   }
@@ -388,7 +400,7 @@ class Tuner {
     }
   }
 
-  struct Result { std::string impl, config; double med, p10, p90; int batch; float err; };
+  struct Result { std::string impl, config; double med = 0, p10 = 0, p90 = 0; int batch = 0; float err = 0; };
 
   void tune_shape(const Shape& s, size_t shape_index) {
     Problem p = make(s);
@@ -413,43 +425,34 @@ class Tuner {
     std::vector<Result> results;
     for (size_t oi = 0; oi < order.size(); ++oi) {
       const std::string& impl = order[oi];
-      // Untimed run + check.
-      CK(cudaMemsetAsync(p.C[0], 0xff, size_t(s.M) * s.N * 2, stream_));  // NaN poison
-      if (!launch(p, impl, 0, p.C[0]) || cudaStreamSynchronize(stream_) != cudaSuccess) {
-        std::fprintf(stderr, "aegis_tune: %dx%dx%d %s: launch failed (%s)\n", s.M, s.N, s.K, impl.c_str(),
-                     aegis_last_error_string());
-        cudaGetLastError();
-        continue;
+      Result res;
+      if (measure(p, s, impl, tol, &res)) {
+        results.push_back(res);
+        emit(s, res, res.impl, p.sets, shape_seed, oi);
       }
-      const float err = impl == "cublas" ? 0.f : max_abs_diff(p, p.C[0]);
-      if (!(err <= tol)) {
-        std::fprintf(stderr, "aegis_tune: %dx%dx%d %s: check failed, max|C - C_cublas| = %g > %g\n", s.M, s.N, s.K,
-                     impl.c_str(), err, tol);
-        continue;
-      }
-      for (int w = 0; w < a_.warmup; ++w) launch(p, impl, w % p.sets, p.C[w % p.sets]);
-      const int batch = calibrate(p, impl);
-      cudaGraphExec_t ge = capture(p, impl, batch);
-      CK(cudaGraphLaunch(ge, stream_));
-      std::vector<double> us;
-      for (int r = 0; r < a_.reps; ++r) us.push_back(time_window(ge, batch));
-      cudaGraphExecDestroy(ge);
-      Result res{impl, config_of(impl), median(us), quantile(us, 0.1), quantile(us, 0.9), batch, err};
-      results.push_back(res);
-      const double flops = 2.0 * s.M * s.N * s.K;
-      const double bytes = 2.0 * (double(s.M) * s.K + double(s.K) * s.N + double(s.M) * s.N);
-      std::printf("{\"kind\":\"measurement\",\"run_id\":\"%s\",\"op\":\"gemm\",\"dtype\":\"%s\",\"m\":%d,\"n\":%d,"
-                  "\"k\":%d,\"impl\":\"%s\",\"config\":%s,\"median_us\":%.4f,\"p10_us\":%.4f,\"p90_us\":%.4f,"
-                  "\"tflops\":%.3f,\"gbps\":%.2f,\"weights_gbps\":%.2f,\"reps\":%d,\"batch_n\":%d,"
-                  "\"buffer_sets\":%d,\"cache_mode\":\"cold\",\"protocol_version\":2,\"checked\":%s,\"pass\":true,"
-                  "\"max_abs_err\":%.6g,\"tol\":%.6g,\"tune\":{\"seed\":%llu,\"shape_seed\":%llu,\"order\":%zu}}\n",
-                  run_id_.c_str(), dname(), s.M, s.N, s.K, impl.c_str(), res.config.c_str(), res.med, res.p10,
-                  res.p90, flops / (res.med * 1e6), bytes / (res.med * 1e3), 2.0 * s.K * s.N / (res.med * 1e3),
-                  a_.reps, batch, p.sets, impl == "cublas" ? "false" : "true", err, tol, a_.seed, shape_seed, oi);
-      std::fflush(stdout);
     }
 
-    // Paired tie tests: fastest config vs runner-up and vs cuBLAS.
+    // cublaslt_best: every kept heuristic candidate, checked and timed the
+    // same way; the fastest is reported.
+    lt_ = std::make_unique<aegis::tune::LtSweep>(a_.dtype == AEGIS_DTYPE_BF16, s.M, s.N, s.K, kLtWorkspace);
+    const Result* lt_best = nullptr;
+    std::vector<Result> lt_results;
+    for (int i = 0; lt_->ok() && i < lt_->size(); ++i) {
+      Result res;
+      if (measure(p, s, "cublaslt#" + std::to_string(i), tol, &res)) lt_results.push_back(res);
+    }
+    for (const Result& r : lt_results)
+      if (!lt_best || r.med < lt_best->med) lt_best = &r;
+    if (lt_best) {
+      Result shown = *lt_best;
+      shown.config = "{\"family\":\"cublaslt\",\"compute\":\"32F\",\"candidates\":" +
+                     std::to_string(lt_->size()) + ",\"dropped_reduced_precision\":" +
+                     std::to_string(lt_->dropped()) + ",\"algo\":" +
+                     lt_->describe(std::atoi(lt_best->impl.c_str() + 9)) + "}";
+      emit(s, shown, "cublaslt_best", p.sets, shape_seed, order.size());
+    }
+
+    // Paired tie tests: fastest config vs runner-up and vs the baselines.
     std::vector<const Result*> ours;
     const Result* base = nullptr;
     for (const Result& r : results) {
@@ -462,12 +465,62 @@ class Tuner {
     if (a_.paired && !ours.empty()) {
       if (ours.size() > 1) paired(p, s, *ours[0], *ours[1], "runner_up", shape_seed);
       if (base) paired(p, s, *ours[0], *base, "cublas", shape_seed + 1);
+      if (lt_best) paired(p, s, *ours[0], *lt_best, "cublaslt_best", shape_seed + 2);
     }
+    lt_.reset();
     release(p);
+  }
+
+  // One configuration: an untimed run checked against cuBLAS, then `reps`
+  // timed windows. False (and a note on stderr) if it fails to launch or
+  // fails the check.
+  bool measure(const Problem& p, const Shape& s, const std::string& impl, double tol, Result* out) {
+    {
+      // Untimed run + check.
+      CK(cudaMemsetAsync(p.C[0], 0xff, size_t(s.M) * s.N * 2, stream_));  // NaN poison
+      if (!launch(p, impl, 0, p.C[0]) || cudaStreamSynchronize(stream_) != cudaSuccess) {
+        std::fprintf(stderr, "aegis_tune: %dx%dx%d %s: launch failed (%s)\n", s.M, s.N, s.K, impl.c_str(),
+                     aegis_last_error_string());
+        cudaGetLastError();
+        return false;
+      }
+    }
+    const float err = impl == "cublas" ? 0.f : max_abs_diff(p, p.C[0]);
+    if (!(err <= tol)) {
+      std::fprintf(stderr, "aegis_tune: %dx%dx%d %s: check failed, max|C - C_cublas| = %g > %g\n", s.M, s.N, s.K,
+                   impl.c_str(), err, tol);
+      return false;
+    }
+    for (int w = 0; w < a_.warmup; ++w) launch(p, impl, w % p.sets, p.C[w % p.sets]);
+    const int batch = calibrate(p, impl);
+    cudaGraphExec_t ge = capture(p, impl, batch);
+    CK(cudaGraphLaunch(ge, stream_));
+    std::vector<double> us;
+    for (int r = 0; r < a_.reps; ++r) us.push_back(time_window(ge, batch));
+    cudaGraphExecDestroy(ge);
+    *out = Result{impl, config_of(impl), median(us), quantile(us, 0.1), quantile(us, 0.9), batch, err};
+    return true;
+  }
+
+  void emit(const Shape& s, const Result& res, const std::string& name, int sets, unsigned long long shape_seed,
+            size_t oi) {
+    const double flops = 2.0 * s.M * s.N * s.K;
+    const double bytes = 2.0 * (double(s.M) * s.K + double(s.K) * s.N + double(s.M) * s.N);
+    const double tol = std::ldexp(1.0, -10) * s.K;
+    std::printf("{\"kind\":\"measurement\",\"run_id\":\"%s\",\"op\":\"gemm\",\"dtype\":\"%s\",\"m\":%d,\"n\":%d,"
+                "\"k\":%d,\"impl\":\"%s\",\"config\":%s,\"median_us\":%.4f,\"p10_us\":%.4f,\"p90_us\":%.4f,"
+                "\"tflops\":%.3f,\"gbps\":%.2f,\"weights_gbps\":%.2f,\"reps\":%d,\"batch_n\":%d,"
+                "\"buffer_sets\":%d,\"cache_mode\":\"cold\",\"protocol_version\":2,\"checked\":%s,\"pass\":true,"
+                "\"max_abs_err\":%.6g,\"tol\":%.6g,\"tune\":{\"seed\":%llu,\"shape_seed\":%llu,\"order\":%zu}}\n",
+                run_id_.c_str(), dname(), s.M, s.N, s.K, name.c_str(), res.config.c_str(), res.med, res.p10,
+                res.p90, flops / (res.med * 1e6), bytes / (res.med * 1e3), 2.0 * s.K * s.N / (res.med * 1e3),
+                a_.reps, res.batch, sets, name == "cublas" ? "false" : "true", res.err, tol, a_.seed, shape_seed, oi);
+    std::fflush(stdout);
   }
 
   std::string config_of(const std::string& impl) const {
     if (impl == "cublas") return "{\"family\":\"cublas\",\"compute\":\"32F\"}";
+    if (impl.rfind("cublaslt#", 0) == 0) return "{\"family\":\"cublaslt\"}";
     for (const Kernel& k : kernels_)
       if (k.name == impl) return k.config.empty() ? "{}" : k.config;
     return "{}";
@@ -505,6 +558,9 @@ class Tuner {
   cublasHandle_t blas_{};
   cudaEvent_t e0_{}, e1_{};
   unsigned* maxdiff_ = nullptr;
+  static constexpr size_t kLtWorkspace = size_t(32) << 20;  // the reference harness's cuBLAS workspace
+  std::unique_ptr<aegis::tune::LtSweep> lt_;
+  void* lt_ws_ = nullptr;
   cudaDeviceProp prop_{};
   std::vector<Kernel> kernels_;
   std::string run_id_;

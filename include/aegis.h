@@ -207,9 +207,17 @@ AEGIS_API int aegis_gemm_bf16_strided_batched(aegis_context* ctx, int layout_a, 
  * finished tile straight into the C of EVERY rank (its own and its peers', over
  * NVLink), so the all-gather of C happens tile by tile inside the GEMM.
  * c_ranks[i] is rank i's C (M x N, row-major, ldc) as a pointer valid on this
- * context's device (aegis_ipc_open_handle for i != rank). After the call, every
- * rank must pass a cross-rank barrier ordered after it on its stream (e.g. a
- * one-element NCCL all-reduce) before any rank reads its C.
+ * context's device (aegis_ipc_open_handle for i != rank).
+ * Ordering, because every rank writes into every rank's C:
+ *   - after the call, every rank must pass a cross-rank barrier ordered after
+ *     it on its stream (e.g. a one-element NCCL all-reduce) before any rank
+ *     reads its C;
+ *   - before a call that writes into a C buffer some rank may still be reading
+ *     (a copy-out of the previous result, a consumer kernel), every rank must
+ *     pass a cross-rank barrier ordered after those reads, or the next call's
+ *     peer stores can overwrite C while it is read. Alternating two C buffers
+ *     does not remove this: the barrier must follow the reads of the buffer
+ *     about to be reused.
  * No counterpart in the reference (it has no multi-GPU code). */
 AEGIS_API int aegis_gemm_bf16_nsharded(aegis_context* ctx, int M, int N, int K, const void* A,
                                        int64_t lda, const void* B_shard, int64_t ldb,

@@ -27,6 +27,8 @@
 // outside stream capture). Later calls only launch: no allocation, no host
 // synchronisation. Never exits: returns cudaSuccess or the error;
 // matmul_last_error() describes the last failure on this host thread.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <span>
@@ -63,8 +65,11 @@ const gemm::KernelEntry* rule_for(const gemm::GemmParams& p, const gemm::DeviceC
 std::span<const Winner> winners_table();
 }  // namespace detail
 
-// Row-major f16 convenience form (reference matmul.h:112-113).
-cudaError_t matmul(const void* A, const void* B, void* C, int M, int N, int K,
+// Row-major f16 convenience form, the reference's signature (matmul.h:112-113).
+cudaError_t matmul(const __half* A, const __half* B, __half* C, int M, int N, int K,
+                   cudaStream_t stream = nullptr);
+// The same for bf16 operands (no reference counterpart: the reference is f16-only).
+cudaError_t matmul(const __nv_bfloat16* A, const __nv_bfloat16* B, __nv_bfloat16* C, int M, int N, int K,
                    cudaStream_t stream = nullptr);
 // General form.
 cudaError_t matmul(const gemm::GemmParams& p, cudaStream_t stream = nullptr);

@@ -31,7 +31,7 @@ def test_reference_arm_line():
     assert line["impl"] == "reference" and line["unit"] == "TFLOP/s" and line["value"] > 0
     assert line["higher_is_better"] is True and line["vs_baseline"] is None
     assert line["steps"] == 2 and line["warmup"] == 1 and line["ms_per_step"] > 0
-    assert line["config"]["workload"] == "config5_gemm_bf16_512^3_nshard"
+    assert line["config"]["workload"] == "gemm_bf16_512^3_nshard"
     cb = line["cpu_baseline"]
     assert cb["value"] == line["value"] and cb["kind"] in ("reference", "port") and cb["cores"] >= 1
     assert "rows" in cb["sample"]
@@ -140,3 +140,23 @@ def test_traffic_comes_from_committed_summaries():
                                         if f.endswith(".traffic.json")))
 def test_every_traffic_summary_is_readable(name):
     assert bench.load_traffic(name) > 0
+
+
+def test_cpu_cost_model_predicts_the_whole_problem():
+    """cpu_reference_rate's extrapolation (fixed + rows x per-row cost, fitted
+    on two row counts of a column block) against one direct call of the
+    reference's CPU GEMM on the whole problem. Loose bounds: a shared CPU."""
+    import time
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import aegis_capi as ac
+    import oracle_py as op
+    n = 1536
+    cb = bench.cpu_reference_rate(n, samples=2, width=512)
+    assert cb["fixed_s"] >= 0 and cb["per_row_s"] > 0 and "fixed" in cb["sample"] and "per row" in cb["sample"]
+    g = ac.Generator(0)
+    A, B = g.uniform(n * n, "f16"), g.uniform(n * n, "f16")
+    d = op.make_desc(n, n, n, dtype="f16")
+    t0 = time.perf_counter()
+    (op.ref_cpu_reference if cb["kind"] == "reference" else op.gemm_ref)(d, A, B)
+    direct = time.perf_counter() - t0
+    assert 0.5 * direct < cb["seconds"] < 2.0 * direct, (cb["seconds"], direct)

@@ -116,3 +116,24 @@ def test_no_device_answers():
     assert lib.aegis_create(ctypes.byref(ctx), 0) == ac.AEGIS_ERR_NO_DEVICE
     assert lib.aegis_hw_info_json(0, None, 0, None) == ac.AEGIS_ERR_NO_DEVICE
     assert lib.aegis_device_manifest(0, None, 0, None) == ac.AEGIS_ERR_NO_DEVICE
+
+
+def test_static_archive_exports_the_cpp_api():
+    """libaegis.a carries the reference's C++ entry points (include/aegis/matmul.h:
+    112-123, include/aegis/gemm.h registry) with their C++ signatures."""
+    from cpp_build import ARCHIVE
+    out = subprocess.run(["nm", "-C", "--defined-only", ARCHIVE], capture_output=True, text=True, check=True).stdout
+    for sym in ["aegis::matmul(__half const*, __half const*, __half*, int, int, int, CUstream_st*)",
+                "aegis::matmul(aegis::gemm::GemmParams const&, CUstream_st*)",
+                "aegis::matmul_choice(int, int, int)", "aegis::matmul_last_error()",
+                "aegis::gemm::registry()", "aegis::gemm::find(std::basic_string_view<char, std::char_traits<char> >)",
+                "aegis_gemm_f16"]:
+        assert re.search(r" T " + re.escape(sym) + r"$", out, re.M), sym
+
+
+def test_cpp_program_links_against_the_static_archive(tmp_path):
+    from cpp_build import build_matmul_test
+    exe = tmp_path / "matmul_test"
+    r = build_matmul_test(str(exe))
+    assert r.returncode == 0, r.stderr[-3000:]
+    assert exe.exists()

@@ -82,3 +82,42 @@ def test_emulated_ranks_ragged_tiles_and_padded_ldc(cuda, nranks):
         got = host(cs[r]).reshape(M, ldc)
         assert np.array_equal(got[:, :N], want), f"rank {r} of {nranks}"
         assert (got[:, N:] == 0x7FC0).all(), "padding columns written"
+
+
+def test_headline_16384_against_the_oracle_and_emulated_ranks(cuda):
+    """The bench's headline workload at its full size: C = A*B, M = N = K =
+    16384, bf16, uniform[-1, 1] from std::mt19937(0), A then B. The 1-rank
+    call's C is checked on 16 sampled rows (0, M-1 and seeded random rows)
+    against the FP64 oracle under both bounds, the size switch of the
+    reference's fuzzer (tools/aegis_fuzz.cu:448); then 8 emulated ranks each
+    store their column shard into all 8 C buffers (4 GiB), and every one must
+    equal the 1-rank result bit for bit (compared on the device)."""
+    import oracle_py as op
+    from gpu_util import check
+    torch = cuda
+    n = 16384
+    g = ac.Generator(0)
+    A, B = g.uniform(n * n, "bf16"), g.uniform(n * n, "bf16")
+    ctx = context(torch)
+    dA, dB = dev(torch, A), dev(torch, B)
+    one = torch.full((n * n,), 0x7FC0, dtype=torch.int16, device="cuda")
+    ctx.nsharded(n, n, n, dA.data_ptr(), n, dB.data_ptr(), n, [one.data_ptr()], n, 1, 0, ac.DTYPE_BF16)
+    ctx.synchronize()
+    rows = sorted({0, n - 1} | set(int(x) for x in np.random.RandomState(20261202).choice(n, 14, replace=False)))
+    got = host(one.view(n, n)[rows].contiguous()).reshape(-1)
+    A_s = np.ascontiguousarray(A.reshape(n, n)[rows]).reshape(-1)
+    d = op.make_desc(len(rows), n, n, dtype="bf16")
+    check(d, A_s, B, None, got, op.gemm_ref(d, A_s, B), name="16384^3 sampled rows")
+
+    P = 8
+    ns = n // P
+    Bm = B.reshape(n, n)
+    cs = [torch.full((n * n,), 0x7E00, dtype=torch.int16, device="cuda") for _ in range(P)]
+    for r in range(P):
+        shard = dev(torch, np.ascontiguousarray(Bm[:, r * ns:(r + 1) * ns]))
+        ctx.nsharded(n, n, n, dA.data_ptr(), n, shard.data_ptr(), ns, [c.data_ptr() for c in cs], n, P, r,
+                     ac.DTYPE_BF16)
+        ctx.synchronize()
+        del shard
+    for r in range(P):
+        assert torch.equal(cs[r], one), f"emulated rank {r} of {P}"

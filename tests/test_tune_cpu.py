@@ -76,6 +76,25 @@ def test_ingest_pick_and_clear_winner(tmp_path, db):
     assert pct == pytest.approx(700.0 / 760.0 * 100)
 
 
+def test_cublaslt_best_is_a_baseline_not_a_winner(tmp_path, db):
+    """A faster cublaslt_best row never becomes the winner; the winner records
+    its percent of cublaslt_best and the paired CI (reference schema.sql:63-68)."""
+    rows = run_rows() + [
+        meas("tune-1", "cublas", 4096, 4096, 4096, 100.0),
+        meas("tune-1", "cublaslt_best", 4096, 4096, 4096, 90.0),
+        meas("tune-1", "umma_256x256x64_s7_c2", 4096, 4096, 4096, 95.0),
+        paired("tune-1", "umma_256x256x64_s7_c2", "cublaslt#2", "cublaslt_best", 4096, 4096, 4096, 0.93, 0.96),
+    ]
+    ap.ingest(db, write(tmp_path, "r.jsonl", rows))
+    assert ap.pick(db, 100) == 1
+    impl, _, _, _, pct = winner(db, "4096x4096x4096")
+    assert impl == "umma_256x256x64_s7_c2" and pct == pytest.approx(100.0 / 95.0 * 100)
+    lt, lo, hi = db.execute("SELECT pct_of_cublaslt_best, lt_ratio_ci_lo, lt_ratio_ci_hi FROM winners").fetchone()
+    assert lt == pytest.approx(90.0 / 95.0 * 100) and (lo, hi) == (0.93, 0.96)
+    text, _ = ap.header_text(db, 100, "x")
+    assert "94.7% of cublaslt_best" in text
+
+
 def test_tie_keeps_the_incumbent_and_ci_swap(tmp_path, db):
     # Run 1: A wins clearly.
     r1 = run_rows("tune-1", "2026-12-01T10:00:00Z") + [
