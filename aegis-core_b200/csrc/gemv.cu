@@ -271,12 +271,21 @@ __global__ void __launch_bounds__(GThreads, gemv_ctas_per_sm(MT)) gemv_kernel(Ge
   __syncthreads();
   if (!s_last) return;
   __threadfence();  // acquire the other CTAs' partials
+  // Slots 0..S-1 summed in order; eight loads in flight at a time (the last
+  // CTA's sum is the kernel's tail).
 #pragma unroll
   for (int r = 0; r < ceil_div(ELEMS, GThreads); ++r) {
     const int e = tid + r * GThreads;
     if (e >= ELEMS) continue;
-    float s = __ldcg(slot0 + e);
-    for (int q = 1; q < a.S; ++q) s += __ldcg(slot0 + (long long)q * ELEMS + e);
+    float s = 0.f;
+    for (int q0 = 0; q0 < a.S; q0 += 8) {
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = q0 + j < a.S ? __ldcg(slot0 + (long long)(q0 + j) * ELEMS + e) : 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (q0 + j < a.S) s = (q0 + j == 0) ? v[j] : s + v[j];
+    }
     store(e, s);
   }
   if (tid == 0) a.counters[tile] = 0;  // ready for the next launch (graph replays need no reset)

@@ -51,12 +51,13 @@ namespace {
 
 std::string umma_name(const UmmaConfig& c) {
   return "umma_" + std::to_string(c.BM) + "x" + std::to_string(c.BN) + "x" + std::to_string(c.BK) + "_s" +
-         std::to_string(c.STAGES) + (c.CTAS == 2 ? "_c2" : "") + (c.SPLITK ? "_ksm" : "");
+         std::to_string(c.STAGES) + (c.CTAS == 2 ? "_c2" : "") + (c.SPLITK ? "_ksm" : "") + (c.KWAVE ? "_kw" : "");
 }
 std::string umma_config(const UmmaConfig& c) {
   return std::string("{\"family\":\"umma\",\"bm\":") + std::to_string(c.BM) + ",\"bn\":" + std::to_string(c.BN) +
          ",\"bk\":" + std::to_string(c.BK) + ",\"stages\":" + std::to_string(c.STAGES) +
-         ",\"cta_group\":" + std::to_string(c.CTAS) + ",\"splitk\":" + (c.SPLITK ? "\"sm\"" : "1") + "}";
+         ",\"cta_group\":" + std::to_string(c.CTAS) + ",\"splitk\":" + (c.SPLITK ? "\"sm\"" : "1") +
+         ",\"k_walk\":" + (c.KWAVE ? "\"by_wave\"" : "\"forward\"") + "}";
 }
 std::string gemv_name(const GemvConfig& c) {
   return "gemv_" + std::to_string(c.BN) + "x" + std::to_string(c.THREADS) + "_ksm";
@@ -99,16 +100,17 @@ cudaError_t simt_launch_rm(const void* A, const void* B, void* C, int M, int N, 
 
 constexpr int kNumUmma = int(sizeof(UMMA_CONFIGS) / sizeof(UMMA_CONFIGS[0]));
 constexpr int kNumGemv = int(sizeof(GEMV_CONFIGS) / sizeof(GEMV_CONFIGS[0]));
-static_assert(kNumUmma == 8 && kNumGemv == 4, "registry tables below list every config row");
+static_assert(kNumUmma == 9 && kNumGemv == 4, "registry tables below list every config row");
 
 const std::vector<KernelEntry>& umma_vec() {
   static const std::vector<KernelEntry> v = [] {
-    const RunFn runs[] = {&umma_run_i<0>, &umma_run_i<1>, &umma_run_i<2>, &umma_run_i<3>,
-                          &umma_run_i<4>, &umma_run_i<5>, &umma_run_i<6>, &umma_run_i<7>};
-    const AttrsFn attrs[] = {&umma_attrs_i<0>, &umma_attrs_i<1>, &umma_attrs_i<2>, &umma_attrs_i<3>,
-                             &umma_attrs_i<4>, &umma_attrs_i<5>, &umma_attrs_i<6>, &umma_attrs_i<7>};
+    const RunFn runs[] = {&umma_run_i<0>, &umma_run_i<1>, &umma_run_i<2>, &umma_run_i<3>, &umma_run_i<4>,
+                          &umma_run_i<5>, &umma_run_i<6>, &umma_run_i<7>, &umma_run_i<8>};
+    const AttrsFn attrs[] = {&umma_attrs_i<0>, &umma_attrs_i<1>, &umma_attrs_i<2>, &umma_attrs_i<3>, &umma_attrs_i<4>,
+                             &umma_attrs_i<5>, &umma_attrs_i<6>, &umma_attrs_i<7>, &umma_attrs_i<8>};
     const LaunchFn launches[] = {&umma_launch_i<0>, &umma_launch_i<1>, &umma_launch_i<2>, &umma_launch_i<3>,
-                                 &umma_launch_i<4>, &umma_launch_i<5>, &umma_launch_i<6>, &umma_launch_i<7>};
+                                 &umma_launch_i<4>, &umma_launch_i<5>, &umma_launch_i<6>, &umma_launch_i<7>,
+                                 &umma_launch_i<8>};
     std::vector<KernelEntry> out;
     for (int i = 0; i < kNumUmma; ++i) {
       const UmmaConfig& c = UMMA_CONFIGS[i];

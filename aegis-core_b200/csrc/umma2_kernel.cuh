@@ -99,7 +99,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const Unit u = decode_unit_pair<BN>(a, first_unit);
     if (a.splits == 1)
       prefetch_first_blocks<A_MN, B_MN, 128, BNH>(&tmA, &tmB, a.M, a.N, a.K, u.m0 + 128 * int(rank),
-                                                u.n0 + BNH * int(rank), u.kb0, min(u.nkb, STAGES),
+                                                u.n0 + BNH * int(rank),
+                                                u.rev ? u.kb0 + u.nkb - min(u.nkb, STAGES) : u.kb0,
+                                                min(u.nkb, STAGES),
                                                 a.a_batched ? u.b : 0, a.b_batched ? u.b : 0);
   }
   if (warp == 1) {
@@ -136,7 +138,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = ptx::mbar_wait_bounded(empty_bar(stage), phase ^ 1u, abort_flag, a.status, kStatusTimeoutProducer,
                                       a.wait_limit_ns);
           if (!ok) break;
-          const int k0 = (u.kb0 + i) * BK;
+          const int k0 = unit_kb(u, i) * BK;
           if (rank == 0) ptx::mbar_arrive_expect_tx(full_bar(stage), 2 * L::STAGE_TX);
           const uint32_t fb = ptx::map_to_rank(full_bar(stage), 0);  // the leader's barrier
           const uint32_t sa = sbase + L::A_OFF + stage * L::A_BYTES;

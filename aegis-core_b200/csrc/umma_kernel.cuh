@@ -71,6 +71,15 @@ struct Args {
   int peer_vec;              // kEpiPeers: 16-byte pushes (aligned bases, ldc and col_offset % 8 == 0)
   unsigned* status;          // per-device watchdog word
   long long wait_limit_ns;
+  // K-walk direction by wave: with kdir_wave > 0 a tile walks its k-blocks
+  // last to first when its position in the full problem's grouped raster
+  // (kdir_tiles_n tile columns, kdir_group rows per group; this launch's
+  // tile column 0 is the full grid's column kdir_col0) lies in an odd wave of
+  // kdir_wave tiles. Consecutive waves then meet at the same end of K, where
+  // the operand blocks the previous wave read last are still in L2. The
+  // direction is a function of the tile and the full problem only, so an
+  // N-sharded rank sums each element in the same order as the 1-GPU GEMM.
+  int kdir_wave, kdir_tiles_n, kdir_col0, kdir_group;
 };
 
 template <int BN, int STAGES>
@@ -94,7 +103,23 @@ struct Layout {
 
 struct Unit {
   int b, m0, n0, split, kb0, nkb;
+  bool rev;  // walk k-blocks kb0 + nkb - 1 down to kb0
 };
+
+// Whether the tile at (tile row mi, tile column ni of this launch) walks K
+// backwards (Args::kdir_wave). Tile counts stay below 2^29 (host-checked).
+__device__ __forceinline__ bool k_reversed(const Args& a, unsigned mi, unsigned ni) {
+  if (a.kdir_wave <= 0) return false;
+  const unsigned g = unsigned(a.kdir_group);
+  const unsigned gn = ni + unsigned(a.kdir_col0);
+  const unsigned grp = mi / g, first_m = grp * g;
+  const unsigned gsize = min(unsigned(a.tiles_m) - first_m, g);
+  const unsigned idx = grp * g * unsigned(a.kdir_tiles_n) + gn * gsize + (mi - first_m);
+  return ((idx / unsigned(a.kdir_wave)) & 1u) != 0;
+}
+
+// The i-th k-block a unit loads (0 <= i < nkb).
+__device__ __forceinline__ int unit_kb(const Unit& u, int i) { return u.kb0 + (u.rev ? u.nkb - 1 - i : i); }
 
 // Unit -> (split, batch, tile) in the grouped raster, for TM-row tiles. Units
 // stay below 2^29 (the host refuses larger plans), so 32-bit unsigned
@@ -125,10 +150,12 @@ __device__ __forceinline__ Unit decode_unit_tm(const Args& a, long long unit) {
   const unsigned gsize = min(unsigned(a.tiles_m) - first_m, unsigned(a.group_m));
   const unsigned rr = t - grp * span;
   const unsigned ni = rr / gsize;
-  r.m0 = int((first_m + (rr - ni * gsize)) * unsigned(TM));
+  const unsigned mi = first_m + (rr - ni * gsize);
+  r.m0 = int(mi * unsigned(TM));
   r.n0 = int(ni * unsigned(BN));
   r.kb0 = r.split * a.kb_per_split;
   r.nkb = min(a.kb_total - r.kb0, a.kb_per_split);
+  r.rev = k_reversed(a, mi, ni);
   return r;
 }
 
@@ -339,7 +366,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // (unsplit walks only: split-K units measured up to 6% slower with it).
     const Unit u = decode_unit<BN>(a, first_unit);
     if (a.splits == 1)
-      prefetch_first_blocks<A_MN, B_MN, BM, BN>(&tmA, &tmB, a.M, a.N, a.K, u.m0, u.n0, u.kb0, min(u.nkb, STAGES),
+      prefetch_first_blocks<A_MN, B_MN, BM, BN>(&tmA, &tmB, a.M, a.N, a.K, u.m0, u.n0,
+                                                u.rev ? u.kb0 + u.nkb - min(u.nkb, STAGES) : u.kb0,
+                                                min(u.nkb, STAGES),
                                               a.a_batched ? u.b : 0, a.b_batched ? u.b : 0);
   }
   if (warp == 1) {
@@ -375,7 +404,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = ptx::mbar_wait_bounded(empty_bar(stage), phase ^ 1u, abort_flag, a.status, kStatusTimeoutProducer,
                                       a.wait_limit_ns);
           if (!ok) break;
-          const int k0 = (u.kb0 + i) * BK;
+          const int k0 = unit_kb(u, i) * BK;
           const uint32_t fb = full_bar(stage);
           ptx::mbar_arrive_expect_tx(fb, L::STAGE_TX);
           const uint32_t sa = sbase + L::A_OFF + stage * L::A_BYTES;

@@ -360,7 +360,14 @@ struct Plan {
   long long total;
 };
 
-// Segments per tile, at most: a CTA covers floor or ceil of T/G k-blocks.
+// The grid G. When s whole-tile splits (s = resident slots / tiles, at
+// least 1) still fill three quarters of the slots, G = tiles * s: CTA c
+// covers [T*c/G, T*(c+1)/G), so every tile is cut into exactly s equal
+// segments, and at s = 1 each CTA streams one whole tile and stores it
+// directly, with no partials and no tickets (M = 1, K x N = 4096 x 14336: 112
+// CTAs, each 1 MB of weights, as cuBLAS's own decode kernel streams it).
+// Otherwise the slots share the k-blocks evenly (stream-K).
+// maxseg: segments per tile, at most (a CTA covers floor or ceil of T/G).
 Plan make_plan(int cfg, const gemm::GemmParams& p) {
   const gemm::UmmavConfig& c = gemm::UMMAV_CONFIGS[cfg];
   Plan pl;
@@ -369,7 +376,12 @@ Plan make_plan(int cfg, const gemm::GemmParams& p) {
   pl.total = (long long)pl.tiles * pl.kb;
   const gpu::Target* d = gpu::planning_target();
   const int sms = d ? d->sms : 148;
-  pl.grid = int(std::max<long long>(1, std::min<long long>(pl.total, (long long)sms * c.CTAS_PER_SM)));
+  const long long slots = (long long)sms * c.CTAS_PER_SM;
+  const long long s = pl.tiles <= slots ? std::min<long long>(slots / pl.tiles, pl.kb) : 0;
+  if (s >= 1 && 4 * pl.tiles * s >= 3 * slots)
+    pl.grid = int(pl.tiles * s);
+  else
+    pl.grid = int(std::max<long long>(1, std::min<long long>(pl.total, slots)));
   const long long per = pl.total / pl.grid;  // smallest range
   pl.maxseg = int(std::min<long long>(pl.grid, (pl.kb + std::max<long long>(1, per) - 1) / std::max<long long>(1, per) + 1));
   return pl;

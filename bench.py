@@ -64,16 +64,17 @@ def parse_args(argv=None):
     p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["aegis", "reference"], default="aegis")
-    p.add_argument("--workload", choices=["nshard", "square", "gemv", "splitk"], default="nshard")
+    p.add_argument("--workload", choices=["nshard", "square", "gemv", "splitk", "gemm"], default="nshard")
     p.add_argument("--size", type=int, default=None, help="square: M=N=K; nshard: M=N=K; splitk: M=N")
-    p.add_argument("--k", type=int, default=None, help="gemv/splitk: K")
-    p.add_argument("--n", type=int, default=None, help="gemv: N")
-    p.add_argument("--m", type=int, default=None, help="gemv: M")
+    p.add_argument("--k", type=int, default=None, help="gemv/splitk/gemm: K")
+    p.add_argument("--n", type=int, default=None, help="gemv/gemm: N")
+    p.add_argument("--m", type=int, default=None, help="gemv/gemm: M")
     p.add_argument("--dtype", choices=["bf16", "f16"], default=None)
     p.add_argument("--kernel", default=None, help="force a registry kernel (single-GPU workloads)")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-workloads", action="store_true", help="skip the secondary single-GPU shapes at N = 1")
+    p.add_argument("--no-lt", action="store_true", help="single-GPU workloads: skip the cublaslt_best sweep")
     a = p.parse_args(argv)
     if a.warmup < 3:
         p.error("--warmup must be >= 3")
@@ -533,14 +534,18 @@ def bench_single(args):
         M = N = args.size or 1024
         K = args.k or 65536
         dtype = args.dtype or "bf16"
+    elif wl == "gemm":  # any M x N x K, uniform[-1, 1]
+        M, N, K = args.m or 16384, args.n or 2048, args.k or 16384
+        dtype = args.dtype or "bf16"
     else:
         M, K, N = args.m or 1, args.k or 4096, args.n or 4096
         dtype = args.dtype or "f16"
     clocks = ClockSampler(0)
     clocks.start()
-    rec = measure_workload(torch, ctx, stream, wl, M, N, K, dtype, args.warmup, impl=args.kernel)
+    rec = measure_workload(torch, ctx, stream, wl, M, N, K, dtype, args.warmup, impl=args.kernel,
+                           lt=not args.no_lt)
     clk = clocks.stop()
-    line = {"metric": {"square": "GEMM TFLOP/s", "splitk": "GEMM TFLOP/s (tall-K split-K)",
+    line = {"metric": {"square": "GEMM TFLOP/s", "splitk": "GEMM TFLOP/s (tall-K split-K)", "gemm": "GEMM TFLOP/s",
                        "gemv": "GEMV HBM GB/s (weights)"}[wl],
             "value": rec["value"], "unit": rec["unit"], "n_gpus": 1, "steps": rec["launches_per_window"],
             "warmup": args.warmup, "ms_per_step": rec["ms"], "higher_is_better": True, "scaling": "weak",

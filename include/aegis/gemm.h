@@ -123,7 +123,10 @@ const KernelEntry* find(std::string_view name);
 // alone cannot fill the GPU (partials reduced in a fixed order, bit-identical
 // across runs). Name: umma_<BM>x<BN>x<BK>_s<STAGES>[_c2][_ksm].
 // ---------------------------------------------------------------------------
-struct UmmaConfig { int BM, BN, BK, STAGES, SPLITK, CTAS; };
+// KWAVE: walk K last to first in every odd wave of resident tiles of the
+// problem's raster, so consecutive waves meet at the same end of K and reuse
+// the operand blocks still in L2 (name suffix _kw).
+struct UmmaConfig { int BM, BN, BK, STAGES, SPLITK, CTAS, KWAVE = 0; };
 // Ring depth of the CTA-pair configs: 7 x 32 KB stages fill the 227 KB of
 // shared memory a CTA may use.
 inline constexpr int kUmmaPairStages = 7;
@@ -138,6 +141,8 @@ inline constexpr UmmaConfig UMMA_CONFIGS[] = {
     // the CTAs of 128 x 128 tiles, and K = 512 fully in flight).
     {128, 64, 64, 8, 0, 1},
     {128, 64, 64, 8, 1, 1},
+    // CTA pairs with the by-wave K walk: less DRAM traffic on multi-wave grids.
+    {256, 256, 64, kUmmaPairStages, 0, 2, 1},
 };
 std::span<const KernelEntry> umma_entries();
 
@@ -185,6 +190,7 @@ struct LaunchPlan {
   int k_chunk = 0;       // K rows per split
   long long tiles = 0;   // output tiles (all batches)
   unsigned grid = 0;     // CTAs launched
+  int kdir_wave = 0;     // umma: tiles per wave of the by-wave k-walk (0: every tile walks K forward)
 };
 bool launch_plan(const char* impl, const GemmParams& p, LaunchPlan* out);
 int split_count(const char* impl, const GemmParams& p);

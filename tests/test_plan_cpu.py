@@ -183,7 +183,7 @@ def test_ummav_plans_fit_the_sms(impl, per_sm, sms):
 MAX_DIM = (1 << 31) - (1 << 20)  # gemm::kMaxDim
 FAMILIES = ["umma_128x256x64_s4", "umma_128x128x64_s6", "umma_128x256x64_s4_ksm", "umma_128x128x64_s6_ksm",
             "umma_256x256x64_s7_c2", "umma_256x256x64_s7_c2_ksm", "umma_128x64x64_s8", "umma_128x64x64_s8_ksm",
-            "gemv_256x256_ksm", "gemv_128x256_ksm", "gemv_64x256_ksm", "gemv_32x256_ksm", "ummav_128x16x64_s11",
+            "umma_256x256x64_s7_c2_kw", "gemv_256x256_ksm", "gemv_128x256_ksm", "gemv_64x256_ksm", "gemv_32x256_ksm", "ummav_128x16x64_s11",
             "ummav_128x16x64_s6x2"]
 
 
@@ -284,3 +284,18 @@ def test_noalloc_plan_refuses_out_of_limit_shapes():
         plan(17, 4096, 4096, impl="gemv_noalloc")
     with pytest.raises(ac.AegisError):
         plan(1, 65537, 4096, impl="gemv_noalloc")
+
+
+@pytest.mark.parametrize("shape", [(16384, 16384, 16384), (8192, 8192, 8192), (1024, 1024, 65536), (512, 512, 512),
+                                   (16384, 2048, 16384), (300, 70000, 1000)])
+def test_k_walk_by_wave_only_on_unsplit_multi_wave_launches(shape):
+    """The _kw pair config walks K by wave (74 resident pairs on 148 SMs) when
+    the launch is unsplit and has more than one wave of tiles; everything else
+    walks K forward."""
+    kw = plan(*shape, impl="umma_256x256x64_s7_c2_kw")
+    fw = plan(*shape, impl="umma_256x256x64_s7_c2")
+    assert (kw["splits"], kw["tiles"], kw["grid"]) == (fw["splits"], fw["tiles"], fw["grid"])
+    assert fw["kdir_wave"] == 0
+    assert kw["kdir_wave"] == (74 if kw["splits"] == 1 and kw["tiles"] > 74 else 0), kw
+    for impl in ["umma_128x256x64_s4", "umma_128x128x64_s6_ksm", "umma_256x256x64_s7_c2_ksm", "umma_128x64x64_s8"]:
+        assert plan(*shape, impl=impl)["kdir_wave"] == 0
