@@ -100,19 +100,17 @@ cudaError_t simt_launch_rm(const void* A, const void* B, void* C, int M, int N, 
 
 constexpr int kNumUmma = int(sizeof(UMMA_CONFIGS) / sizeof(UMMA_CONFIGS[0]));
 constexpr int kNumGemv = int(sizeof(GEMV_CONFIGS) / sizeof(GEMV_CONFIGS[0]));
-static_assert(kNumUmma == 11 && kNumGemv == 4, "registry tables below list every config row");
+static_assert(kNumUmma == 9 && kNumGemv == 4, "registry tables below list every config row");
 
 const std::vector<KernelEntry>& umma_vec() {
   static const std::vector<KernelEntry> v = [] {
-    const RunFn runs[] = {&umma_run_i<0>, &umma_run_i<1>, &umma_run_i<2>, &umma_run_i<3>,
-                          &umma_run_i<4>, &umma_run_i<5>, &umma_run_i<6>, &umma_run_i<7>,
-                          &umma_run_i<8>, &umma_run_i<9>, &umma_run_i<10>};
-    const AttrsFn attrs[] = {&umma_attrs_i<0>, &umma_attrs_i<1>, &umma_attrs_i<2>, &umma_attrs_i<3>,
-                             &umma_attrs_i<4>, &umma_attrs_i<5>, &umma_attrs_i<6>, &umma_attrs_i<7>,
-                             &umma_attrs_i<8>, &umma_attrs_i<9>, &umma_attrs_i<10>};
+    const RunFn runs[] = {&umma_run_i<0>, &umma_run_i<1>, &umma_run_i<2>, &umma_run_i<3>, &umma_run_i<4>,
+                          &umma_run_i<5>, &umma_run_i<6>, &umma_run_i<7>, &umma_run_i<8>};
+    const AttrsFn attrs[] = {&umma_attrs_i<0>, &umma_attrs_i<1>, &umma_attrs_i<2>, &umma_attrs_i<3>, &umma_attrs_i<4>,
+                             &umma_attrs_i<5>, &umma_attrs_i<6>, &umma_attrs_i<7>, &umma_attrs_i<8>};
     const LaunchFn launches[] = {&umma_launch_i<0>, &umma_launch_i<1>, &umma_launch_i<2>, &umma_launch_i<3>,
                                  &umma_launch_i<4>, &umma_launch_i<5>, &umma_launch_i<6>, &umma_launch_i<7>,
-                                 &umma_launch_i<8>, &umma_launch_i<9>, &umma_launch_i<10>};
+                                 &umma_launch_i<8>};
     std::vector<KernelEntry> out;
     for (int i = 0; i < kNumUmma; ++i) {
       const UmmaConfig& c = UMMA_CONFIGS[i];

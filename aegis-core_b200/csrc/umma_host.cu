@@ -357,9 +357,7 @@ cudaError_t umma_attrs(int cfg, cudaFuncAttributes* attrs) {
 
 size_t umma_smem_bytes(int cfg) {
   const gemm::UmmaConfig& c = gemm::UMMA_CONFIGS[cfg];
-  if (c.CTAS == 2)
-    return c.BN == 128 ? size_t(umma::LayoutPair<128, gemm::kUmmaPair128Stages>::ALLOC)
-                       : size_t(umma::LayoutPair<256, gemm::kUmmaPairStages>::ALLOC);
+  if (c.CTAS == 2) return size_t(umma::LayoutPair<256, gemm::kUmmaPairStages>::ALLOC);
   if (c.BN == 64) return size_t(umma::Layout<64, 8>::ALLOC);
   return c.BN == 256 ? size_t(umma::Layout<256, 4>::ALLOC) : size_t(umma::Layout<128, 6>::ALLOC);
 }

@@ -100,15 +100,13 @@ cudaError_t launch_epi(const LaunchKey& k, const CUtensorMap& ta, const CUtensor
 }
 
 // The instantiations the registry lists (gemm::UMMA_CONFIGS): one CTA (256, 4),
-// (128, 6) and (64, 8); CTA pairs (256, gemm::kUmmaPairStages) and
-// (128, gemm::kUmmaPair128Stages).
+// (128, 6) and (64, 8); CTA pairs (256, gemm::kUmmaPairStages).
 template <class T>
 cudaError_t launch_family(const LaunchKey& k, const CUtensorMap& ta, const CUtensorMap& tb, const Args& a,
                           int grid, cudaStream_t s) {
   if (k.pair) {
-    constexpr int PS = gemm::kUmmaPairStages, PS128 = gemm::kUmmaPair128Stages;
+    constexpr int PS = gemm::kUmmaPairStages;
     if (k.BN == 256 && k.STAGES == PS) return launch_epi<T, 256, PS, true>(k, ta, tb, a, grid, s);
-    if (k.BN == 128 && k.STAGES == PS128) return launch_epi<T, 128, PS128, true>(k, ta, tb, a, grid, s);
     return cudaErrorNotSupported;
   }
   if (k.BN == 256 && k.STAGES == 4) return launch_epi<T, 256, 4, false>(k, ta, tb, a, grid, s);
@@ -119,15 +117,10 @@ cudaError_t launch_family(const LaunchKey& k, const CUtensorMap& ta, const CUten
 
 template <class T>
 cudaError_t attrs_family(int BN, int STAGES, bool pair, cudaFuncAttributes* attrs) {
-  constexpr int PS = gemm::kUmmaPairStages, PS128 = gemm::kUmmaPair128Stages;
+  constexpr int PS = gemm::kUmmaPairStages;
   if (pair && BN == 256 && STAGES == PS) {
     const cudaError_t e = cudaFuncGetAttributes(attrs, &umma2_gemm_kernel<T, 256, PS, false, true, kEpiStore>);
     if (e == cudaSuccess) attrs->sharedSizeBytes += LayoutPair<256, PS>::ALLOC;
-    return e;
-  }
-  if (pair && BN == 128 && STAGES == PS128) {
-    const cudaError_t e = cudaFuncGetAttributes(attrs, &umma2_gemm_kernel<T, 128, PS128, false, true, kEpiStore>);
-    if (e == cudaSuccess) attrs->sharedSizeBytes += LayoutPair<128, PS128>::ALLOC;
     return e;
   }
   if (BN == 256 && STAGES == 4) return attrs_one<T, 256, 4, false, true, kEpiStore>(attrs);

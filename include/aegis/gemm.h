@@ -130,10 +130,6 @@ struct UmmaConfig { int BM, BN, BK, STAGES, SPLITK, CTAS, KWAVE = 0; };
 // Ring depth of the CTA-pair configs: 7 x 32 KB stages fill the 227 KB of
 // shared memory a CTA may use.
 inline constexpr int kUmmaPairStages = 7;
-// 256 x 128 pair tiles: 24 KB stages (A 16 KB + B 8 KB per CTA), 9 deep.
-// Twice the tiles of 256 x 256 for the same shape: fewer idle pairs in the
-// last wave (4096^3: 512 tiles = 6.9 waves of 74 pairs against 3.5).
-inline constexpr int kUmmaPair128Stages = 9;
 inline constexpr UmmaConfig UMMA_CONFIGS[] = {
     {128, 256, 64, 4, 0, 1},
     {128, 128, 64, 6, 0, 1},
@@ -147,8 +143,6 @@ inline constexpr UmmaConfig UMMA_CONFIGS[] = {
     {128, 64, 64, 8, 1, 1},
     // CTA pairs with the by-wave K walk: less DRAM traffic on multi-wave grids.
     {256, 256, 64, kUmmaPairStages, 0, 2, 1},
-    {256, 128, 64, kUmmaPair128Stages, 0, 2},
-    {256, 128, 64, kUmmaPair128Stages, 1, 2},
 };
 std::span<const KernelEntry> umma_entries();
 

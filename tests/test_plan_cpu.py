@@ -139,7 +139,7 @@ def test_gemv_plans_are_one_wave(impl, sms):
 
 
 SPLIT_IMPLS = {"umma_128x256x64_s4_ksm": 1, "umma_128x128x64_s6_ksm": 1, "umma_256x256x64_s7_c2_ksm": 2,
-               "umma_128x64x64_s8_ksm": 1, "umma_256x128x64_s9_c2_ksm": 2}
+               "umma_128x64x64_s8_ksm": 1}
 TALL_K = [(256, 256, 65536), (512, 512, 65536), (1024, 1024, 65536), (300, 200, 30001), (129, 136, 7777),
           (16, 4096, 14336), (1, 14336, 4096)]
 
@@ -183,7 +183,7 @@ def test_ummav_plans_fit_the_sms(impl, per_sm, sms):
 MAX_DIM = (1 << 31) - (1 << 20)  # gemm::kMaxDim
 FAMILIES = ["umma_128x256x64_s4", "umma_128x128x64_s6", "umma_128x256x64_s4_ksm", "umma_128x128x64_s6_ksm",
             "umma_256x256x64_s7_c2", "umma_256x256x64_s7_c2_ksm", "umma_128x64x64_s8", "umma_128x64x64_s8_ksm",
-            "umma_256x256x64_s7_c2_kw", "umma_256x128x64_s9_c2", "umma_256x128x64_s9_c2_ksm", "gemv_256x256_ksm", "gemv_128x256_ksm", "gemv_64x256_ksm", "gemv_32x256_ksm", "ummav_128x16x64_s11",
+            "umma_256x256x64_s7_c2_kw", "gemv_256x256_ksm", "gemv_128x256_ksm", "gemv_64x256_ksm", "gemv_32x256_ksm", "ummav_128x16x64_s11",
             "ummav_128x16x64_s6x2"]
 
 

@@ -15,7 +15,7 @@ from gpu_util import check, context, dev, host, run
 pytestmark = pytest.mark.gpu
 
 SPLIT_IMPLS = ["umma_128x256x64_s4_ksm", "umma_128x128x64_s6_ksm", "umma_256x256x64_s7_c2_ksm",
-               "umma_128x64x64_s8_ksm", "umma_256x128x64_s9_c2_ksm"]
+               "umma_128x64x64_s8_ksm"]
 
 
 @pytest.mark.parametrize("mn", [256, 512, 1024])
