@@ -382,13 +382,17 @@ Plan make_plan(int cfg, const gemm::GemmParams& p) {
     pl.grid = int(pl.tiles * s);
   else
     pl.grid = int(std::max<long long>(1, std::min<long long>(pl.total, slots)));
+  // A clustered launch needs whole clusters; any grid is a valid partition
+  // (the ranges stay contiguous and cover every k-block), possibly with fix-ups.
+  if (c.CLUSTER > 1) pl.grid = int(ceil_div<long long>(pl.grid, c.CLUSTER) * c.CLUSTER);
   const long long per = pl.total / pl.grid;  // smallest range
   pl.maxseg = int(std::min<long long>(pl.grid, (pl.kb + std::max<long long>(1, per) - 1) / std::max<long long>(1, per) + 1));
   return pl;
 }
 
 template <class T, int STAGES>
-cudaError_t launch_s(const CUtensorMap& ta, const CUtensorMap& tb, const Args& a, int grid, cudaStream_t s) {
+cudaError_t launch_s(const CUtensorMap& ta, const CUtensorMap& tb, const Args& a, int grid, int cluster,
+                     cudaStream_t s) {
   auto* kern = &ummav_kernel<T, STAGES>;
   static gpu::SmemOptIn optin;
   constexpr size_t smem = size_t(Layout<STAGES>::ALLOC);
@@ -401,20 +405,24 @@ cudaError_t launch_s(const CUtensorMap& ta, const CUtensorMap& tb, const Args& a
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = unsigned(cluster);
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = cluster > 1 ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, kern, ta, tb, a);
 }
 
 // The instantiations gemm::UMMAV_CONFIGS lists.
 template <class T>
-cudaError_t launch(int stages, const CUtensorMap& ta, const CUtensorMap& tb, const Args& a, int grid,
+cudaError_t launch(int stages, const CUtensorMap& ta, const CUtensorMap& tb, const Args& a, int grid, int cluster,
                    cudaStream_t s) {
-  if (stages == 11) return launch_s<T, 11>(ta, tb, a, grid, s);
-  if (stages == 6) return launch_s<T, 6>(ta, tb, a, grid, s);
+  if (stages == 11) return launch_s<T, 11>(ta, tb, a, grid, cluster, s);
+  if (stages == 6) return launch_s<T, 6>(ta, tb, a, grid, cluster, s);
   return cudaErrorNotSupported;
 }
 
@@ -469,9 +477,10 @@ cudaError_t ummav_run(int cfg, const gemm::GemmParams& p, cudaStream_t stream) {
     a.counters = static_cast<unsigned*>(cnt);
     a.partials = static_cast<float*>(part);
   }
-  const int stages = gemm::UMMAV_CONFIGS[cfg].STAGES;
-  return p.dtype == gemm::DType::BF16 ? ummav::launch<__nv_bfloat16>(stages, ta, tb, a, pl.grid, stream)
-                                      : ummav::launch<__half>(stages, ta, tb, a, pl.grid, stream);
+  const gemm::UmmavConfig& c = gemm::UMMAV_CONFIGS[cfg];
+  return p.dtype == gemm::DType::BF16
+             ? ummav::launch<__nv_bfloat16>(c.STAGES, ta, tb, a, pl.grid, c.CLUSTER, stream)
+             : ummav::launch<__half>(c.STAGES, ta, tb, a, pl.grid, c.CLUSTER, stream);
 }
 
 gemm::LaunchPlan ummav_plan(int cfg, const gemm::GemmParams& p) {

@@ -818,8 +818,8 @@ def e2e_pipelined(torch, dist, ctx, args, world, rank, M, N, K, ns, c0, A, B_sha
             dBs[j].copy_(hB, non_blocking=True)
             ev_in[j].record(s_in)
         stream.wait_event(ev_in[j])
-        if world > 1:
-            dist.all_gather_into_tensor(dAs[j], dAs[j][r0 * K:(r0 + h) * K])
+        if world > 1:  # bytes only: any 16-bit type NCCL takes
+            dist.all_gather_into_tensor(dAs[j].view(torch.bfloat16), dAs[j][r0 * K:(r0 + h) * K].view(torch.bfloat16))
         stream.wait_event(ev_out[j])  # this rank's read-back of C[j] (step i-2) is done
         if world > 1:
             dist.all_reduce(flag)  # ... and every other rank's: C[j] is free everywhere

@@ -167,10 +167,15 @@ std::span<const KernelEntry> gemv_entries();
 // all CTAs (stream-K segments) with an ordered ticket fix-up. Deterministic.
 // Name: ummav_128x16x64_s<STAGES>[x<CTAS_PER_SM>].
 // ---------------------------------------------------------------------------
-struct UmmavConfig { int STAGES, CTAS_PER_SM; };
+// CLUSTER: CTAs launched as one thread-block cluster (co-scheduled on one GPC;
+// no shared memory or barrier crosses CTAs). Consecutive CTAs stream
+// neighbouring 128-column weight strips, so a cluster of four reads 1 KB of
+// each weight row at about the same time (name suffix _c4).
+struct UmmavConfig { int STAGES, CTAS_PER_SM, CLUSTER = 1; };
 inline constexpr UmmavConfig UMMAV_CONFIGS[] = {
     {11, 1},
     {6, 2},
+    {11, 1, 4},
 };
 std::span<const KernelEntry> ummav_entries();
 

@@ -171,20 +171,30 @@ def test_unsplit_configs_never_split():
 
 
 @pytest.mark.parametrize("sms", [148, 132])
-@pytest.mark.parametrize("impl,per_sm", [("ummav_128x16x64_s11", 1), ("ummav_128x16x64_s6x2", 2)])
-def test_ummav_plans_fit_the_sms(impl, per_sm, sms):
+@pytest.mark.parametrize("impl,per_sm,cluster", [("ummav_128x16x64_s11", 1, 1), ("ummav_128x16x64_s6x2", 2, 1),
+                                                 ("ummav_128x16x64_s11_c4", 1, 4)])
+def test_ummav_plans_fit_the_sms(impl, per_sm, cluster, sms):
+    """Grids stay within the resident slots (rounded up to whole clusters) and
+    the k-block count; when whole-tile splits fill 3/4 of the slots, the grid
+    is tiles x s, so no tile is cut unevenly."""
     for (M, N, K) in DECODE:
         p = plan(M, N, K, impl, sms=sms)
         kb = math.ceil(K / 64)
-        assert p["tiles"] == math.ceil(N / 128), p
-        assert 1 <= p["grid"] <= min(per_sm * sms, p["tiles"] * kb), p
+        tiles = math.ceil(N / 128)
+        slots = per_sm * sms
+        assert p["tiles"] == tiles, p
+        assert p["grid"] % cluster == 0, p
+        assert 1 <= p["grid"] <= math.ceil(min(slots, tiles * kb) / cluster) * cluster, p
+        s = min(slots // tiles, kb) if tiles <= slots else 0
+        if s >= 1 and 4 * tiles * s >= 3 * slots and (tiles * s) % cluster == 0:
+            assert p["grid"] == tiles * s, p
 
 
 MAX_DIM = (1 << 31) - (1 << 20)  # gemm::kMaxDim
 FAMILIES = ["umma_128x256x64_s4", "umma_128x128x64_s6", "umma_128x256x64_s4_ksm", "umma_128x128x64_s6_ksm",
             "umma_256x256x64_s7_c2", "umma_256x256x64_s7_c2_ksm", "umma_128x64x64_s8", "umma_128x64x64_s8_ksm",
             "umma_256x256x64_s7_c2_kw", "gemv_256x256_ksm", "gemv_128x256_ksm", "gemv_64x256_ksm", "gemv_32x256_ksm", "ummav_128x16x64_s11",
-            "ummav_128x16x64_s6x2"]
+            "ummav_128x16x64_s6x2", "ummav_128x16x64_s11_c4"]
 
 
 def test_random_plans_keep_their_invariants():
