@@ -80,6 +80,14 @@ struct Args {
   // direction is a function of the tile and the full problem only, so an
   // N-sharded rank sums each element in the same order as the 1-GPU GEMM.
   int kdir_wave, kdir_tiles_n, kdir_col0, kdir_group;
+  // Tail split (kEpiStore launches with splits == 1): the tiles from raster
+  // position tail_first on (the partial last wave) are each cut into
+  // tail_splits K slices of tail_kb k-blocks, one unit each, so the idle
+  // slots of the last wave share them. A slice writes FP32 partials to
+  // tail_part[(tile - tail_first) * tail_splits + slice][tail_tm][BN]; a
+  // second kernel sums the slices in order (deterministic).
+  int tail_first, tail_splits, tail_kb, tail_tm;
+  float* tail_part;
 };
 
 template <int BN, int STAGES>
@@ -103,7 +111,8 @@ struct Layout {
 
 struct Unit {
   int b, m0, n0, split, kb0, nkb;
-  bool rev;  // walk k-blocks kb0 + nkb - 1 down to kb0
+  bool rev;   // walk k-blocks kb0 + nkb - 1 down to kb0
+  int slot;   // >= 0: a tail slice, written as FP32 partials to this tail_part slot
 };
 
 // Whether the tile at (tile row mi, tile column ni of this launch) walks K
@@ -126,22 +135,18 @@ __device__ __forceinline__ int unit_kb(const Unit& u, int i) { return u.kb0 + (u
 // arithmetic is exact; the split and batch divisions are skipped when there is
 // one of them (a 64-bit division by a run-time value is a long emulated
 // sequence, measured at ~0.7 us before a small GEMM's first load).
+// Raster position `tile` (batch-major, then the grouped raster of each batch
+// entry) -> batch, first row and first column; returns the tile's (row,
+// column) index in the grid through mi, ni.
 template <int TM, int BN>
-__device__ __forceinline__ Unit decode_unit_tm(const Args& a, long long unit) {
-  const unsigned u = unsigned(unit);
-  Unit r;
-  unsigned tile = u;
-  r.split = 0;
-  if (a.splits > 1) {
-    tile = u / unsigned(a.splits);
-    r.split = int(u - tile * unsigned(a.splits));
-  }
+__device__ __forceinline__ void decode_tile_tm(const Args& a, unsigned tile, Unit* r, unsigned* mi_out,
+                                               unsigned* ni_out) {
   unsigned t = tile;
-  r.b = 0;
+  r->b = 0;
   if (a.batch > 1) {
     const unsigned per_batch = unsigned(a.tiles_m) * unsigned(a.tiles_n);
     const unsigned b = tile / per_batch;
-    r.b = int(b);
+    r->b = int(b);
     t = tile - b * per_batch;
   }
   const unsigned span = unsigned(a.group_m) * unsigned(a.tiles_n);
@@ -151,8 +156,36 @@ __device__ __forceinline__ Unit decode_unit_tm(const Args& a, long long unit) {
   const unsigned rr = t - grp * span;
   const unsigned ni = rr / gsize;
   const unsigned mi = first_m + (rr - ni * gsize);
-  r.m0 = int(mi * unsigned(TM));
-  r.n0 = int(ni * unsigned(BN));
+  r->m0 = int(mi * unsigned(TM));
+  r->n0 = int(ni * unsigned(BN));
+  *mi_out = mi;
+  *ni_out = ni;
+}
+
+template <int TM, int BN>
+__device__ __forceinline__ Unit decode_unit_tm(const Args& a, long long unit) {
+  const unsigned u = unsigned(unit);
+  Unit r;
+  unsigned tile = u, mi = 0, ni = 0;
+  r.split = 0;
+  r.slot = -1;
+  r.rev = false;
+  if (a.tail_splits > 1 && u >= unsigned(a.tail_first)) {
+    // A slice of a tail tile: raster position tail_first + q / tail_splits.
+    const unsigned q = u - unsigned(a.tail_first);
+    const unsigned t = q / unsigned(a.tail_splits);
+    const unsigned sl = q - t * unsigned(a.tail_splits);
+    r.slot = int(q);
+    r.kb0 = int(sl) * a.tail_kb;
+    r.nkb = min(a.kb_total - r.kb0, a.tail_kb);
+    decode_tile_tm<TM, BN>(a, unsigned(a.tail_first) + t, &r, &mi, &ni);
+    return r;
+  }
+  if (a.splits > 1) {
+    tile = u / unsigned(a.splits);
+    r.split = int(u - tile * unsigned(a.splits));
+  }
+  decode_tile_tm<TM, BN>(a, tile, &r, &mi, &ni);
   r.kb0 = r.split * a.kb_per_split;
   r.nkb = min(a.kb_total - r.kb0, a.kb_per_split);
   r.rev = k_reversed(a, mi, ni);
@@ -215,7 +248,7 @@ __device__ __forceinline__ void store_row_chunk(T* dst, const float (&v)[32], in
   }
 }
 
-template <class T, int EPI>
+template <class T, int EPI, int BN_TAIL>
 __device__ __forceinline__ void epilogue_chunk(const Args& a, const Unit& u, int row, int col,
                                                const uint32_t (&r)[32]) {
   using E = Elem<T>;
@@ -235,6 +268,15 @@ __device__ __forceinline__ void epilogue_chunk(const Args& a, const Unit& u, int
         if (i < ncols) dst[i] = v[i];
     }
   } else if constexpr (EPI == kEpiStore) {
+    if (u.slot >= 0) {  // a tail slice: FP32 partials, summed by tail_reduce_kernel
+      float* dst = a.tail_part + ((long long)u.slot * a.tail_tm + (row - u.m0)) * BN_TAIL + (col - u.n0);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+      float4* d4 = reinterpret_cast<float4*>(dst);  // 128-byte aligned: col - n0 is a multiple of 32
+#pragma unroll
+      for (int q = 0; q < 8; ++q) d4[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      return;
+    }
     T* dst = static_cast<T*>(a.C) + (long long)u.b * a.stride_c + (long long)row * a.ldc + col;
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = a.alpha * __uint_as_float(r[i]);
@@ -314,11 +356,11 @@ __device__ __forceinline__ void drain_rows(const Args& a, const Unit& u, int row
     ptx::tmem_ld_wait(r0);
     ptx::tmem_ld_32x32b_x32(t_row + uint32_t((c + 1) * 32), r1);
     const int col0 = u.n0 + c * 32;
-    if (row < a.M && col0 < a.N) epilogue_chunk<T, EPI>(a, u, row, col0, r0);
+    if (row < a.M && col0 < a.N) epilogue_chunk<T, EPI, BN>(a, u, row, col0, r0);
     ptx::tmem_ld_wait(r1);
     if (c + 2 < BN / 32) ptx::tmem_ld_32x32b_x32(t_row + uint32_t((c + 2) * 32), r0);
     const int col1 = col0 + 32;
-    if (row < a.M && col1 < a.N) epilogue_chunk<T, EPI>(a, u, row, col1, r1);
+    if (row < a.M && col1 < a.N) epilogue_chunk<T, EPI, BN>(a, u, row, col1, r1);
   }
 }
 

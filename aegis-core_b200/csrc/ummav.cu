@@ -382,9 +382,12 @@ Plan make_plan(int cfg, const gemm::GemmParams& p) {
     pl.grid = int(pl.tiles * s);
   else
     pl.grid = int(std::max<long long>(1, std::min<long long>(pl.total, slots)));
-  // A clustered launch needs whole clusters; any grid is a valid partition
-  // (the ranges stay contiguous and cover every k-block), possibly with fix-ups.
-  if (c.CLUSTER > 1) pl.grid = int(ceil_div<long long>(pl.grid, c.CLUSTER) * c.CLUSTER);
+  // A clustered launch needs whole clusters: round the grid down (never up:
+  // with more CTAs than k-blocks some ranges would be empty, and the segment
+  // and ticket accounting counts every CTA between a tile's first and last
+  // owner). Any grid up to the k-block count is a valid partition, possibly
+  // with fix-ups. Fewer CTAs than one cluster launch unclustered.
+  if (c.CLUSTER > 1 && pl.grid >= c.CLUSTER) pl.grid = pl.grid / c.CLUSTER * c.CLUSTER;
   const long long per = pl.total / pl.grid;  // smallest range
   pl.maxseg = int(std::min<long long>(pl.grid, (pl.kb + std::max<long long>(1, per) - 1) / std::max<long long>(1, per) + 1));
   return pl;
@@ -478,9 +481,10 @@ cudaError_t ummav_run(int cfg, const gemm::GemmParams& p, cudaStream_t stream) {
     a.partials = static_cast<float*>(part);
   }
   const gemm::UmmavConfig& c = gemm::UMMAV_CONFIGS[cfg];
+  const int cluster = pl.grid % c.CLUSTER == 0 ? c.CLUSTER : 1;
   return p.dtype == gemm::DType::BF16
-             ? ummav::launch<__nv_bfloat16>(c.STAGES, ta, tb, a, pl.grid, c.CLUSTER, stream)
-             : ummav::launch<__half>(c.STAGES, ta, tb, a, pl.grid, c.CLUSTER, stream);
+             ? ummav::launch<__nv_bfloat16>(c.STAGES, ta, tb, a, pl.grid, cluster, stream)
+             : ummav::launch<__half>(c.STAGES, ta, tb, a, pl.grid, cluster, stream);
 }
 
 gemm::LaunchPlan ummav_plan(int cfg, const gemm::GemmParams& p) {

@@ -196,6 +196,8 @@ struct LaunchPlan {
   long long tiles = 0;   // output tiles (all batches)
   unsigned grid = 0;     // CTAs launched
   int kdir_wave = 0;     // umma: tiles per wave of the by-wave k-walk (0: every tile walks K forward)
+  int tail_splits = 0;   // umma split-K configs: K slices of each tile of a partial last wave (0: none)
+  long long tail_tiles = 0;  // ... and how many tiles that wave holds
 };
 bool launch_plan(const char* impl, const GemmParams& p, LaunchPlan* out);
 int split_count(const char* impl, const GemmParams& p);
