@@ -159,8 +159,13 @@ def test_tail_split_matches_oracle_and_the_unsplit_tiles(cuda, case, impl, ref_i
     assert all(np.array_equal(o, outs[0]) for o in outs), "tail split differs run to run"
     dC = dev(torch, C0)
     run(torch, ctx, d, dA, dB, dC, ref_impl)
-    whole = host(dC).reshape(M, ldc)
-    got = outs[0].reshape(M, ldc)
+
+    def rows_of(flat):  # C spans (M - 1) * ldc + N elements: pad the last row to ldc
+        full = np.zeros(M * ldc, np.uint16)
+        full[:flat.size] = flat
+        return full.reshape(M, ldc)
+    whole = rows_of(host(dC))
+    got = rows_of(outs[0])
     # Which output rows/columns lie in tail tiles: recompute the grouped raster.
     tm = 256 if "_c2" in impl else 128
     bn = 256
@@ -186,8 +191,8 @@ def test_tail_split_matches_oracle_and_the_unsplit_tiles(cuda, case, impl, ref_i
         A_rows = np.concatenate([A2[r * lda:r * lda + K] for r in rows])
     else:
         A_rows = np.concatenate([A2[np.arange(K) * lda + r] for r in rows])
-    C0_rows = np.concatenate([C0[r * ldc:r * ldc + ldc] for r in rows])
+    C0_rows = rows_of(C0)[rows].reshape(-1)
     sub = op.make_desc(len(rows), N, K, 0, lb, K, ldb, ldc, alpha, beta, 1, 0, 0, 0, dtype)
     ref = op.gemm_ref(sub, A_rows, B, C0_rows if beta != 0 else None)
-    out_rows = np.concatenate([outs[0][r * ldc:r * ldc + ldc] for r in rows])
+    out_rows = got[rows].reshape(-1)
     check(sub, A_rows, B, C0_rows, out_rows, ref, f"{impl} tail rows {case}")
