@@ -404,9 +404,8 @@ int aegis_gemm_plan_json(aegis_context* ctx, const char* impl, int dtype, int M,
   if (!aegis::gemm::find(name)) return fail_arg(fn, "no such kernel configuration in the registry");
   if (!aegis::gemm::launch_plan(name, p, &pl)) pl = aegis::gemm::LaunchPlan{};
   char b[384];
-  std::snprintf(b, sizeof b, "{\"impl\":\"%s\",\"splits\":%d,\"k_chunk\":%d,\"tiles\":%lld,\"grid\":%u,\"kdir_wave\":%d,"
-                "\"tail_splits\":%d,\"tail_tiles\":%lld}", name,
-                pl.splits, pl.k_chunk, pl.tiles, pl.grid, pl.kdir_wave, pl.tail_splits, pl.tail_tiles);
+  std::snprintf(b, sizeof b, "{\"impl\":\"%s\",\"splits\":%d,\"k_chunk\":%d,\"tiles\":%lld,\"grid\":%u,\"kdir_wave\":%d}", name,
+                pl.splits, pl.k_chunk, pl.tiles, pl.grid, pl.kdir_wave);
   return copy_out(b, buf, buf_len, needed);
 }
 
@@ -445,10 +444,9 @@ int aegis_plan_simulated_json(int arch, int sm_count, const char* impl, int dtyp
   }
   char b[384];
   std::snprintf(b, sizeof b,
-                "{\"impl\":\"%s\",\"splits\":%d,\"k_chunk\":%d,\"tiles\":%lld,\"grid\":%u,\"kdir_wave\":%d,"
-                "\"tail_splits\":%d,\"tail_tiles\":%lld,\"dispatch\":\"%s\","
+                "{\"impl\":\"%s\",\"splits\":%d,\"k_chunk\":%d,\"tiles\":%lld,\"grid\":%u,\"kdir_wave\":%d,\"dispatch\":\"%s\","
                 "\"kind\":\"%s\"}",
-                name, pl.splits, pl.k_chunk, pl.tiles, pl.grid, pl.kdir_wave, pl.tail_splits, pl.tail_tiles, chosen,
+                name, pl.splits, pl.k_chunk, pl.tiles, pl.grid, pl.kdir_wave, chosen,
                 c.kind == aegis::detail::Choice::Kind::Aegis ? "winner" : "rule");
   return copy_out(b, buf, buf_len, needed);
 }

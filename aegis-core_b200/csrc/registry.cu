@@ -157,12 +157,12 @@ cudaError_t ummav_launch_i(const void* A, const void* B, void* C, int M, int N, 
 
 const std::vector<KernelEntry>& ummav_vec() {
   static const std::vector<KernelEntry> v = [] {
-    static_assert(sizeof(UMMAV_CONFIGS) / sizeof(UMMAV_CONFIGS[0]) == 3, "ummav table below lists every row");
-    const RunFn runs[] = {&ummav_run_i<0>, &ummav_run_i<1>, &ummav_run_i<2>};
-    const AttrsFn attrs[] = {&ummav_attrs_i<0>, &ummav_attrs_i<1>, &ummav_attrs_i<2>};
-    const LaunchFn launches[] = {&ummav_launch_i<0>, &ummav_launch_i<1>, &ummav_launch_i<2>};
+    static_assert(sizeof(UMMAV_CONFIGS) / sizeof(UMMAV_CONFIGS[0]) == 2, "ummav table below lists every row");
+    const RunFn runs[] = {&ummav_run_i<0>, &ummav_run_i<1>};
+    const AttrsFn attrs[] = {&ummav_attrs_i<0>, &ummav_attrs_i<1>};
+    const LaunchFn launches[] = {&ummav_launch_i<0>, &ummav_launch_i<1>};
     std::vector<KernelEntry> out;
-    for (int i = 0; i < 3; ++i) {
+    for (int i = 0; i < 2; ++i) {
       const UmmavConfig& c = UMMAV_CONFIGS[i];
       KernelReq req;
       req.min_arch = 100;
@@ -171,12 +171,10 @@ const std::vector<KernelEntry>& ummav_vec() {
       req.smem_bytes = ummav_smem_bytes(i);
       req.threads = 192;
       const std::string name = "ummav_128x16x64_s" + std::to_string(c.STAGES) +
-                               (c.CTAS_PER_SM > 1 ? "x" + std::to_string(c.CTAS_PER_SM) : std::string()) +
-                               (c.CLUSTER > 1 ? "_c" + std::to_string(c.CLUSTER) : std::string());
+                               (c.CTAS_PER_SM > 1 ? "x" + std::to_string(c.CTAS_PER_SM) : std::string());
       const std::string cfg = std::string("{\"family\":\"ummav\",\"bm\":128,\"bn\":16,\"bk\":64,\"stages\":") +
                               std::to_string(c.STAGES) + ",\"cta_group\":1,\"ctas_per_sm\":" +
-                              std::to_string(c.CTAS_PER_SM) + ",\"cluster\":" + std::to_string(c.CLUSTER) +
-                              ",\"split\":\"stream-k\"}";
+                              std::to_string(c.CTAS_PER_SM) + ",\"split\":\"stream-k\"}";
       out.push_back({keep(name), keep(cfg), launches[i], attrs[i], runs[i], 16, req});
     }
     return out;

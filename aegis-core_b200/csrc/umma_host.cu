@@ -140,57 +140,6 @@ cudaError_t launch_reduce(const float* part, int S, const GemmParams& p, cudaStr
                                   p.stride_c, p.alpha, p.beta);
 }
 
-// ---------------------------------------------------------------- tail reduce
-// The slices of the tail tiles (umma::Args::tail_*): C = alpha * (slice 0 +
-// slice 1 + ... ) (+ beta * C) over each tail tile, slices summed in order.
-// Block (t, y): tail tile t, rows y*256/BN .. of its TM x BN partials, four
-// columns per thread.
-template <class T, int TM, int BN>
-__global__ void __launch_bounds__(256) tail_reduce_kernel(const __grid_constant__ umma::Args a) {
-  using E = Elem<T>;
-  ptx::griddep_wait();  // launched as a programmatic dependent of the GEMM that wrote the slices
-  ptx::griddep_launch_dependents();
-  constexpr int kElems = TM * BN;
-  const unsigned t = blockIdx.x;
-  umma::Unit u;
-  unsigned mi = 0, ni = 0;
-  umma::decode_tile_tm<TM, BN>(a, unsigned(a.tail_first) + t, &u, &mi, &ni);
-  const float4* base = reinterpret_cast<const float4*>(a.tail_part + (long long)t * a.tail_splits * kElems);
-  T* C = static_cast<T*>(a.C);
-  for (int e = (int(blockIdx.y) * 256 + int(threadIdx.x)) * 4; e < kElems; e += int(gridDim.y) * 256 * 4) {
-    const int row = u.m0 + e / BN, col = u.n0 + e % BN;
-    if (row >= a.M || col >= a.N) continue;
-    const float4 acc = sum_slots4(base + e / 4, kElems / 4, a.tail_splits);  // in slice order
-    const float s4[4] = {acc.x, acc.y, acc.z, acc.w};
-    T* c = C + (long long)row * a.ldc + col;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      if (col + j >= a.N) break;
-      float v = a.alpha * s4[j];
-      if (a.beta != 0.f) v += a.beta * E::to_f32(c[j]);
-      c[j] = E::from_f32(v);
-    }
-  }
-}
-
-template <class T>
-cudaError_t launch_tail_reduce(const umma::Args& a, int tail_tiles, int TM, int BN, cudaStream_t s) {
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(unsigned(tail_tiles), 16u);
-  cfg.blockDim = dim3(256);
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  if (TM == 256 && BN == 256) return cudaLaunchKernelEx(&cfg, &tail_reduce_kernel<T, 256, 256>, a);
-  if (TM == 128 && BN == 256) return cudaLaunchKernelEx(&cfg, &tail_reduce_kernel<T, 128, 256>, a);
-  if (TM == 128 && BN == 128) return cudaLaunchKernelEx(&cfg, &tail_reduce_kernel<T, 128, 128>, a);
-  if (TM == 128 && BN == 64) return cudaLaunchKernelEx(&cfg, &tail_reduce_kernel<T, 128, 64>, a);
-  return cudaErrorNotSupported;
-}
-
 // ---------------------------------------------------------------- planning
 // Units one launch can take (one cluster each, grid.x < 2^31). Far above
 // any problem that fits in device memory; larger plans are refused.
@@ -206,7 +155,6 @@ struct Plan {
   int grid = 0;
   int slots = 0;      // units resident at once (CTAs, or pairs for cta_group::2)
   bool kwave = false;  // the config walks K by wave (UmmaConfig::KWAVE)
-  int tail_first = 0, tail_splits = 0, tail_kb = 0;  // tail split (umma::Args::tail_*)
 };
 
 // Raster group (tile rows walked together before moving along N): 8, or 4
@@ -306,20 +254,6 @@ Plan make_plan(int cfg, const GemmParams& p) {
   pl.kb_per_split = ceil_div(pl.kb_total, S);
   pl.splits = ceil_div(pl.kb_total, pl.kb_per_split);
   pl.units = pl.tiles * pl.splits;
-  // Tail split: when the tiles fill whole waves of the slots plus a partial
-  // one at most half full, the split-K configs cut each tile of that last
-  // wave into st >= 2 K slices (at least 4 k-blocks each), so all the slots
-  // share it (4096^3 on 74 pairs: 34 tail tiles -> 68 half tiles).
-  if (c.SPLITK && S == 1 && sms > 0 && pl.tiles > sms && p.batch == 1) {
-    const long long tail = pl.tiles % sms;
-    const long long st = tail > 0 ? std::min<long long>(sms / tail, pl.kb_total / 4) : 0;
-    if (st >= 2) {
-      pl.tail_kb = ceil_div(pl.kb_total, int(st));
-      pl.tail_splits = ceil_div(pl.kb_total, pl.tail_kb);
-      pl.tail_first = int(pl.tiles - tail);
-      pl.units = (pl.tiles - tail) + tail * pl.tail_splits;
-    }
-  }
   // One CTA (pair: one cluster of two) per unit: the CTAs that fit run and
   // take the rest in launch order (tile_sched.cuh).
   pl.grid = int(std::max<long long>(1, std::min<long long>(pl.units, kMaxUnits))) * c.CTAS;
@@ -354,10 +288,6 @@ umma::Args make_args(const GemmParams& p, const Plan& pl) {
   a.beta = p.beta;
   a.wait_limit_ns = kDefaultWaitLimitNs;
   set_kdir(&a, pl, p.batch, pl.tiles_n, 0);
-  a.tail_first = pl.tail_first;
-  a.tail_splits = pl.tail_splits;
-  a.tail_kb = pl.tail_kb;
-  a.tail_tm = pl.BM;
   return a;
 }
 
@@ -395,18 +325,6 @@ cudaError_t umma_run(int cfg, const GemmParams& p, cudaStream_t stream) {
   if (const cudaError_t e = status::word(&a.status); e != cudaSuccess) return e;
   umma::LaunchKey k{pl.BN, pl.STAGES, p.layout_a == Layout::ColMajor, p.layout_b == Layout::RowMajor,
                     umma::kEpiStore, pl.CTAS == 2};
-  if (pl.tail_splits > 1) {
-    // Tail slices' partials, then their ordered sum into C.
-    const int tail_tiles = int(pl.tiles - pl.tail_first);
-    void* part = nullptr;
-    const size_t bytes = size_t(tail_tiles) * pl.tail_splits * pl.BM * pl.BN * sizeof(float);
-    if (const cudaError_t e = scratch::acquire(stream, bytes, scratch::Kind::Partials, &part); e != cudaSuccess)
-      return e;
-    a.tail_part = static_cast<float*>(part);
-    if (const cudaError_t e = launch(p, k, maps, a, pl.grid, stream); e != cudaSuccess) return e;
-    return p.dtype == DType::BF16 ? launch_tail_reduce<__nv_bfloat16>(a, tail_tiles, pl.BM, pl.BN, stream)
-                                  : launch_tail_reduce<__half>(a, tail_tiles, pl.BM, pl.BN, stream);
-  }
   if (pl.splits == 1) return launch(p, k, maps, a, pl.grid, stream);
   // Split-K: partials, then the ordered reduction.
   void* part = nullptr;
@@ -429,8 +347,6 @@ gemm::LaunchPlan umma_plan(int cfg, const GemmParams& p) {
   umma::Args a{};
   set_kdir(&a, pl, p.batch, pl.tiles_n, 0);
   r.kdir_wave = a.kdir_wave;
-  r.tail_splits = pl.tail_splits;
-  r.tail_tiles = pl.tail_splits > 1 ? pl.tiles - pl.tail_first : 0;
   return r;
 }
 

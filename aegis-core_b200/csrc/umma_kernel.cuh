@@ -80,14 +80,6 @@ struct Args {
   // direction is a function of the tile and the full problem only, so an
   // N-sharded rank sums each element in the same order as the 1-GPU GEMM.
   int kdir_wave, kdir_tiles_n, kdir_col0, kdir_group;
-  // Tail split (kEpiStore launches with splits == 1): the tiles from raster
-  // position tail_first on (the partial last wave) are each cut into
-  // tail_splits K slices of tail_kb k-blocks, one unit each, so the idle
-  // slots of the last wave share them. A slice writes FP32 partials to
-  // tail_part[(tile - tail_first) * tail_splits + slice][tail_tm][BN]; a
-  // second kernel sums the slices in order (deterministic).
-  int tail_first, tail_splits, tail_kb, tail_tm;
-  float* tail_part;
 };
 
 template <int BN, int STAGES>
@@ -111,8 +103,7 @@ struct Layout {
 
 struct Unit {
   int b, m0, n0, split, kb0, nkb;
-  bool rev;   // walk k-blocks kb0 + nkb - 1 down to kb0
-  int slot;   // >= 0: a tail slice, written as FP32 partials to this tail_part slot
+  bool rev;  // walk k-blocks kb0 + nkb - 1 down to kb0
 };
 
 // Whether the tile at (tile row mi, tile column ni of this launch) walks K
@@ -168,19 +159,7 @@ __device__ __forceinline__ Unit decode_unit_tm(const Args& a, long long unit) {
   Unit r;
   unsigned tile = u, mi = 0, ni = 0;
   r.split = 0;
-  r.slot = -1;
   r.rev = false;
-  if (a.tail_splits > 1 && u >= unsigned(a.tail_first)) {
-    // A slice of a tail tile: raster position tail_first + q / tail_splits.
-    const unsigned q = u - unsigned(a.tail_first);
-    const unsigned t = q / unsigned(a.tail_splits);
-    const unsigned sl = q - t * unsigned(a.tail_splits);
-    r.slot = int(q);
-    r.kb0 = int(sl) * a.tail_kb;
-    r.nkb = min(a.kb_total - r.kb0, a.tail_kb);
-    decode_tile_tm<TM, BN>(a, unsigned(a.tail_first) + t, &r, &mi, &ni);
-    return r;
-  }
   if (a.splits > 1) {
     tile = u / unsigned(a.splits);
     r.split = int(u - tile * unsigned(a.splits));
@@ -248,7 +227,7 @@ __device__ __forceinline__ void store_row_chunk(T* dst, const float (&v)[32], in
   }
 }
 
-template <class T, int EPI, int BN_TAIL>
+template <class T, int EPI>
 __device__ __forceinline__ void epilogue_chunk(const Args& a, const Unit& u, int row, int col,
                                                const uint32_t (&r)[32]) {
   using E = Elem<T>;
@@ -268,15 +247,6 @@ __device__ __forceinline__ void epilogue_chunk(const Args& a, const Unit& u, int
         if (i < ncols) dst[i] = v[i];
     }
   } else if constexpr (EPI == kEpiStore) {
-    if (u.slot >= 0) {  // a tail slice: FP32 partials, summed by tail_reduce_kernel
-      float* dst = a.tail_part + ((long long)u.slot * a.tail_tm + (row - u.m0)) * BN_TAIL + (col - u.n0);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-      float4* d4 = reinterpret_cast<float4*>(dst);  // 128-byte aligned: col - n0 is a multiple of 32
-#pragma unroll
-      for (int q = 0; q < 8; ++q) d4[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-      return;
-    }
     T* dst = static_cast<T*>(a.C) + (long long)u.b * a.stride_c + (long long)row * a.ldc + col;
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = a.alpha * __uint_as_float(r[i]);
@@ -356,11 +326,11 @@ __device__ __forceinline__ void drain_rows(const Args& a, const Unit& u, int row
     ptx::tmem_ld_wait(r0);
     ptx::tmem_ld_32x32b_x32(t_row + uint32_t((c + 1) * 32), r1);
     const int col0 = u.n0 + c * 32;
-    if (row < a.M && col0 < a.N) epilogue_chunk<T, EPI, BN>(a, u, row, col0, r0);
+    if (row < a.M && col0 < a.N) epilogue_chunk<T, EPI>(a, u, row, col0, r0);
     ptx::tmem_ld_wait(r1);
     if (c + 2 < BN / 32) ptx::tmem_ld_32x32b_x32(t_row + uint32_t((c + 2) * 32), r0);
     const int col1 = col0 + 32;
-    if (row < a.M && col1 < a.N) epilogue_chunk<T, EPI, BN>(a, u, row, col1, r1);
+    if (row < a.M && col1 < a.N) epilogue_chunk<T, EPI>(a, u, row, col1, r1);
   }
 }
 

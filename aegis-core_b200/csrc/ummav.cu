@@ -382,20 +382,13 @@ Plan make_plan(int cfg, const gemm::GemmParams& p) {
     pl.grid = int(pl.tiles * s);
   else
     pl.grid = int(std::max<long long>(1, std::min<long long>(pl.total, slots)));
-  // A clustered launch needs whole clusters: round the grid down (never up:
-  // with more CTAs than k-blocks some ranges would be empty, and the segment
-  // and ticket accounting counts every CTA between a tile's first and last
-  // owner). Any grid up to the k-block count is a valid partition, possibly
-  // with fix-ups. Fewer CTAs than one cluster launch unclustered.
-  if (c.CLUSTER > 1 && pl.grid >= c.CLUSTER) pl.grid = pl.grid / c.CLUSTER * c.CLUSTER;
   const long long per = pl.total / pl.grid;  // smallest range
   pl.maxseg = int(std::min<long long>(pl.grid, (pl.kb + std::max<long long>(1, per) - 1) / std::max<long long>(1, per) + 1));
   return pl;
 }
 
 template <class T, int STAGES>
-cudaError_t launch_s(const CUtensorMap& ta, const CUtensorMap& tb, const Args& a, int grid, int cluster,
-                     cudaStream_t s) {
+cudaError_t launch_s(const CUtensorMap& ta, const CUtensorMap& tb, const Args& a, int grid, cudaStream_t s) {
   auto* kern = &ummav_kernel<T, STAGES>;
   static gpu::SmemOptIn optin;
   constexpr size_t smem = size_t(Layout<STAGES>::ALLOC);
@@ -408,24 +401,20 @@ cudaError_t launch_s(const CUtensorMap& ta, const CUtensorMap& tb, const Args& a
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[2];
+  cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
-  attr[1].id = cudaLaunchAttributeClusterDimension;
-  attr[1].val.clusterDim.x = unsigned(cluster);
-  attr[1].val.clusterDim.y = 1;
-  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = cluster > 1 ? 2 : 1;
+  cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kern, ta, tb, a);
 }
 
 // The instantiations gemm::UMMAV_CONFIGS lists.
 template <class T>
-cudaError_t launch(int stages, const CUtensorMap& ta, const CUtensorMap& tb, const Args& a, int grid, int cluster,
+cudaError_t launch(int stages, const CUtensorMap& ta, const CUtensorMap& tb, const Args& a, int grid,
                    cudaStream_t s) {
-  if (stages == 11) return launch_s<T, 11>(ta, tb, a, grid, cluster, s);
-  if (stages == 6) return launch_s<T, 6>(ta, tb, a, grid, cluster, s);
+  if (stages == 11) return launch_s<T, 11>(ta, tb, a, grid, s);
+  if (stages == 6) return launch_s<T, 6>(ta, tb, a, grid, s);
   return cudaErrorNotSupported;
 }
 
@@ -480,11 +469,9 @@ cudaError_t ummav_run(int cfg, const gemm::GemmParams& p, cudaStream_t stream) {
     a.counters = static_cast<unsigned*>(cnt);
     a.partials = static_cast<float*>(part);
   }
-  const gemm::UmmavConfig& c = gemm::UMMAV_CONFIGS[cfg];
-  const int cluster = pl.grid % c.CLUSTER == 0 ? c.CLUSTER : 1;
-  return p.dtype == gemm::DType::BF16
-             ? ummav::launch<__nv_bfloat16>(c.STAGES, ta, tb, a, pl.grid, cluster, stream)
-             : ummav::launch<__half>(c.STAGES, ta, tb, a, pl.grid, cluster, stream);
+  const int stages = gemm::UMMAV_CONFIGS[cfg].STAGES;
+  return p.dtype == gemm::DType::BF16 ? ummav::launch<__nv_bfloat16>(stages, ta, tb, a, pl.grid, stream)
+                                      : ummav::launch<__half>(stages, ta, tb, a, pl.grid, stream);
 }
 
 gemm::LaunchPlan ummav_plan(int cfg, const gemm::GemmParams& p) {

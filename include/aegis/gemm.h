@@ -167,15 +167,10 @@ std::span<const KernelEntry> gemv_entries();
 // all CTAs (stream-K segments) with an ordered ticket fix-up. Deterministic.
 // Name: ummav_128x16x64_s<STAGES>[x<CTAS_PER_SM>].
 // ---------------------------------------------------------------------------
-// CLUSTER: CTAs launched as one thread-block cluster (co-scheduled on one GPC;
-// no shared memory or barrier crosses CTAs). Consecutive CTAs stream
-// neighbouring 128-column weight strips, so a cluster of four reads 1 KB of
-// each weight row at about the same time (name suffix _c4).
-struct UmmavConfig { int STAGES, CTAS_PER_SM, CLUSTER = 1; };
+struct UmmavConfig { int STAGES, CTAS_PER_SM; };
 inline constexpr UmmavConfig UMMAV_CONFIGS[] = {
     {11, 1},
     {6, 2},
-    {11, 1, 4},
 };
 std::span<const KernelEntry> ummav_entries();
 
@@ -196,8 +191,6 @@ struct LaunchPlan {
   long long tiles = 0;   // output tiles (all batches)
   unsigned grid = 0;     // CTAs launched
   int kdir_wave = 0;     // umma: tiles per wave of the by-wave k-walk (0: every tile walks K forward)
-  int tail_splits = 0;   // umma split-K configs: K slices of each tile of a partial last wave (0: none)
-  long long tail_tiles = 0;  // ... and how many tiles that wave holds
 };
 bool launch_plan(const char* impl, const GemmParams& p, LaunchPlan* out);
 int split_count(const char* impl, const GemmParams& p);

@@ -21,7 +21,7 @@ pytestmark = pytest.mark.gpu
 
 IMPLS = ["umma_128x256x64_s4", "umma_128x128x64_s6", "umma_128x256x64_s4_ksm", "umma_128x128x64_s6_ksm",
          "umma_256x256x64_s7_c2", "umma_256x256x64_s7_c2_ksm", "umma_128x64x64_s8", "umma_128x64x64_s8_ksm",
-         "umma_256x256x64_s7_c2_kw", "gemv_256x256_ksm", "gemv_128x256_ksm", "gemv_64x256_ksm", "gemv_32x256_ksm", "ummav_128x16x64_s11", "ummav_128x16x64_s6x2", "ummav_128x16x64_s11_c4",
+         "umma_256x256x64_s7_c2_kw", "gemv_256x256_ksm", "gemv_128x256_ksm", "gemv_64x256_ksm", "gemv_32x256_ksm", "ummav_128x16x64_s11", "ummav_128x16x64_s6x2",
          "simt_64x64x16"]
 
 

@@ -120,79 +120,3 @@ def test_graph_capture_after_first_call(cuda):
                                dB.data_ptr(), N, 0, 0.0, dC.data_ptr(), N, 0, 1)
             assert e.value.status == ac.AEGIS_ERR_CUDA
 
-
-# Shapes whose tiles fill whole waves plus a last wave at most half full, so
-# the split-K configs cut each tile of that last wave into K slices:
-# (M, N, K, layout_a, layout_b, alpha, beta, ldc pad, dtype).
-TAIL_CASES = [(2560, 2560, 512, 0, 0, 1.0, 0.0, 0, "bf16"),     # pairs: 100 tiles, 26 tail tiles x 2
-              (2600, 2500, 1000, 0, 0, 1.0, 0.0, 3, "f16"),     # ragged edges, padded ldc
-              (2560, 2560, 768, 1, 1, -0.5, 0.75, 0, "bf16"),   # col-major operands, alpha/beta
-              (4096, 4096, 1024, 0, 0, 1.0, 0.0, 0, "bf16")]    # the 4096^3 tile grid: 34 tail tiles x 2
-
-
-@pytest.mark.parametrize("case", TAIL_CASES, ids=lambda c: f"{c[0]}x{c[1]}x{c[2]}_{c[8]}")
-@pytest.mark.parametrize("impl,ref_impl", [("umma_256x256x64_s7_c2_ksm", "umma_256x256x64_s7_c2"),
-                                           ("umma_128x256x64_s4_ksm", "umma_128x256x64_s4")])
-def test_tail_split_matches_oracle_and_the_unsplit_tiles(cuda, case, impl, ref_impl):
-    """The tail tiles' K slices, summed in order by the tail reduce kernel:
-    bitwise identical over 3 runs; sampled rows of every tail tile within both
-    bounds of the FP64 oracle; every tile outside the tail bitwise equal to
-    the same config without split-K (the same kernel and K order)."""
-    torch = cuda
-    M, N, K, la, lb, alpha, beta, pad, dtype = case
-    ctx = context(torch)
-    plan = ctx.plan(M, N, K, impl, ac.DTYPE_BF16 if dtype == "bf16" else ac.DTYPE_F16)
-    assert plan["tail_splits"] >= 2 and plan["tail_tiles"] > 0, plan
-    lda = K if la == 0 else M
-    ldb = N if lb == 0 else K
-    ldc = N + pad
-    d = op.make_desc(M, N, K, la, lb, lda, ldb, ldc, alpha, beta, 1, 0, 0, 0, dtype)
-    na, nb, nc = op.spans(d)
-    g = ac.Generator(M * 3 + K)
-    A, B, C0 = g.uniform(na, dtype), g.uniform(nb, dtype), g.uniform(nc, dtype)
-    dA, dB = dev(torch, A), dev(torch, B)
-    outs = []
-    for _ in range(3):
-        dC = dev(torch, C0)
-        run(torch, ctx, d, dA, dB, dC, impl)
-        outs.append(host(dC))
-    assert all(np.array_equal(o, outs[0]) for o in outs), "tail split differs run to run"
-    dC = dev(torch, C0)
-    run(torch, ctx, d, dA, dB, dC, ref_impl)
-
-    def rows_of(flat):  # C spans (M - 1) * ldc + N elements: pad the last row to ldc
-        full = np.zeros(M * ldc, np.uint16)
-        full[:flat.size] = flat
-        return full.reshape(M, ldc)
-    whole = rows_of(host(dC))
-    got = rows_of(outs[0])
-    # Which output rows/columns lie in tail tiles: recompute the grouped raster.
-    tm = 256 if "_c2" in impl else 128
-    bn = 256
-    tiles_m, tiles_n = -(-M // tm), -(-N // bn)
-    group = 8
-    tail_first = tiles_m * tiles_n - plan["tail_tiles"]
-    in_tail = np.zeros((M, N), dtype=bool)
-    for t in range(tail_first, tiles_m * tiles_n):
-        grp = t // (group * tiles_n)
-        first_m = grp * group
-        gsize = min(tiles_m - first_m, group)
-        rr = t - grp * group * tiles_n
-        ni, mi = rr // gsize, first_m + rr % gsize
-        in_tail[mi * tm:(mi + 1) * tm, ni * bn:(ni + 1) * bn] = True
-    assert in_tail.any() and not in_tail.all()
-    assert np.array_equal(got[:, :N][~in_tail], whole[:, :N][~in_tail]), "a non-tail tile differs from the unsplit run"
-    assert np.array_equal(got[:, N:], whole[:, N:]), "padding columns written"
-    tail_rows = np.nonzero(in_tail.any(axis=1))[0]
-    rows = sorted(set(int(r) for r in np.random.RandomState(M).choice(tail_rows, 12, replace=False)) |
-                  {int(tail_rows[0]), int(tail_rows[-1])})
-    A2 = A.reshape(-1)
-    if la == 0:
-        A_rows = np.concatenate([A2[r * lda:r * lda + K] for r in rows])
-    else:
-        A_rows = np.concatenate([A2[np.arange(K) * lda + r] for r in rows])
-    C0_rows = rows_of(C0)[rows].reshape(-1)
-    sub = op.make_desc(len(rows), N, K, 0, lb, K, ldb, ldc, alpha, beta, 1, 0, 0, 0, dtype)
-    ref = op.gemm_ref(sub, A_rows, B, C0_rows if beta != 0 else None)
-    out_rows = got[rows].reshape(-1)
-    check(sub, A_rows, B, C0_rows, out_rows, ref, f"{impl} tail rows {case}")
