@@ -59,47 +59,31 @@ inline constexpr long long kDefaultWaitLimitNs = 2000000000ll;
 
 // Split-K slot sums: p[0] + p[stride] + ... + p[(S-1)*stride] in that fixed
 // order (the first slot taken as is, each next one added, exactly as a plain
-// sequential loop does), with the L2 loads issued eight at a time so S slots
-// cost about S/8 round trips instead of S.
-__device__ __forceinline__ float sum_slots(const float* p, long long stride, int S) {
-  float acc = 0.f;
-  int q = 0;
-  for (; q + 8 <= S; q += 8) {
-    float v[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = __ldcg(p + (long long)(q + j) * stride);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) acc = (q + j == 0) ? v[j] : acc + v[j];
+// sequential loop does), with the L2 loads issued BATCH at a time (the last
+// batch predicated) so S slots cost ceil(S/BATCH) round trips instead of S.
+// BATCH = 8 for floats, 4 for float4 (16 data registers in flight, so a
+// reduce kernel keeps its occupancy).
+__device__ __forceinline__ void add_slot(float& acc, float v, bool first) { acc = first ? v : acc + v; }
+__device__ __forceinline__ void add_slot(float4& acc, const float4& v, bool first) {
+  if (first) {
+    acc = v;
+  } else {
+    acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
   }
-  for (; q < S; ++q) {
-    const float v = __ldcg(p + (long long)q * stride);
-    acc = (q == 0) ? v : acc + v;
-  }
-  return acc;
 }
-__device__ __forceinline__ float4 sum_slots4(const float4* p, long long stride, int S) {
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  int q = 0;
-  for (; q + 8 <= S; q += 8) {
-    float4 v[8];
+// `stride` and S * stride fit in 32 bits (split-K workspaces are capped far
+// below 2^31 elements).
+template <class V, int BATCH = sizeof(V) == 16 ? 4 : 8>
+__device__ __forceinline__ V sum_slots_t(const V* p, int stride, int S) {
+  V acc{};
+  for (int q = 0; q < S; q += BATCH, p += BATCH * stride) {
+    V v[BATCH];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = __ldcg(p + (long long)(q + j) * stride);
+    for (int j = 0; j < BATCH; ++j)
+      if (q + j < S) v[j] = __ldcg(p + j * stride);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      if (q + j == 0) {
-        acc = v[j];
-      } else {
-        acc.x += v[j].x; acc.y += v[j].y; acc.z += v[j].z; acc.w += v[j].w;
-      }
-    }
-  }
-  for (; q < S; ++q) {
-    const float4 v = __ldcg(p + (long long)q * stride);
-    if (q == 0) {
-      acc = v;
-    } else {
-      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
-    }
+    for (int j = 0; j < BATCH; ++j)
+      if (q + j < S) add_slot(acc, v[j], q + j == 0);
   }
   return acc;
 }

@@ -14,6 +14,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 #include "gpu_target.h"
@@ -73,43 +74,78 @@ bool make_maps(const GemmParams& p, int bbox, Maps* m) {
 }
 
 // ---------------------------------------------------------------- split-K reduce
-// out[b][m][n] = alpha * (P[0] + P[1] + ... + P[S-1]) (+ beta * C), summed in
-// split order. Four columns per thread when N % 4 == 0.
+// out[b][m][n] = alpha * (P[0] + ... + P[S-1]) (+ beta * C) in a fixed order:
+// the S slots form G consecutive groups of per = ceil(S/G) slots; each group is
+// summed in slot order by its own threads, then the group sums are added in
+// group order. G is the smallest power of two with per <= 8, at most 8, so a
+// group costs one batch of L2 loads up to S = 64. G and the order depend on S
+// only: results are bitwise identical run to run and on every rank of an
+// N-sharded call. A block is 256 threads = G groups x 256/G units (float4 when
+// N % 4 == 0, else float).
+constexpr int kReduceThreads = 256;
+constexpr int kReduceMaxGroups = 8;
+
+inline int reduce_groups(int S) {
+  int G = 1;
+  while (G < kReduceMaxGroups && (S + G - 1) / G > 8) G *= 2;
+  return G;
+}
+
 template <class T, bool VEC4>
-__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ part, int S, int batch, int M,
-                                                            int N, T* __restrict__ C, long long ldc,
-                                                            long long stride_c, float alpha, float beta) {
+__global__ void __launch_bounds__(kReduceThreads, 4) splitk_reduce_kernel(const float* __restrict__ part, int S,
+                                                                       int lg_groups, int batch, int M, int N,
+                                                                       T* __restrict__ C, long long ldc,
+                                                                       long long stride_c, float alpha, float beta) {
   using E = Elem<T>;
+  using V = std::conditional_t<VEC4, float4, float>;
+  constexpr int W = VEC4 ? 4 : 1;
+  __shared__ V group_sum[kReduceThreads];
   // Launched as a programmatic dependent of the GEMM that wrote the partials:
   // nothing is read before that grid has completed.
   ptx::griddep_wait();
   ptx::griddep_launch_dependents();
-  const long long plane = (long long)batch * M * N;
-  constexpr int W = VEC4 ? 4 : 1;
+  // 32-bit indexing: the host guarantees S * batch * M * N < 2^31.
+  const int plane_v = batch * M * N / W;  // one slot, in V units
   const int nw = N / W;
-  const long long total = (long long)batch * M * nw;
-  for (long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x; t < total;
-       t += (long long)gridDim.x * blockDim.x) {
-    const int n = int(t % nw) * W;
-    const long long bm = t / nw;
-    const int m = int(bm % M), b = int(bm / M);
-    const long long off = bm * N + n;
+  const int total = plane_v;
+  const int G = 1 << lg_groups;
+  const int U = kReduceThreads >> lg_groups;  // units per pass
+  const int per = (S + G - 1) / G;
+  const int g = int(threadIdx.x) >> (8 - lg_groups), u = int(threadIdx.x) & (U - 1);
+  const int q0 = g * per, q1 = min(S, q0 + per);
+  const V* base = reinterpret_cast<const V*>(part) + q0 * plane_v;
+  for (int t = int(blockIdx.x) * U + u, t_end = ((total + U - 1) / U) * U; t < t_end; t += int(gridDim.x) * U) {
+    V acc{};
+    // Partials are dense [S][batch][M][N]: unit t of slot q is base[q * plane_v + t].
+    if (t < total && q0 < q1) acc = sum_slots_t<V>(base + t, plane_v, q1 - q0);
+    if (G > 1) {  // block-uniform
+      group_sum[threadIdx.x] = acc;
+      __syncthreads();
+      if (g == 0) {
+        for (int k = 1; k < G && k * per < S; ++k) add_slot(acc, group_sum[k * U + u], false);
+      }
+      __syncthreads();  // group_sum is reused by the next pass
+    }
+    if (g != 0 || t >= total) continue;
+    const int bm = t / nw, n = (t - bm * nw) * W;
+    const int m = bm % M, b = bm / M;
     T* c = C + b * stride_c + (long long)m * ldc + n;
     if constexpr (VEC4) {
-      const float4 acc = sum_slots4(reinterpret_cast<const float4*>(part + off), plane / 4, S);  // in split order
       float v[4] = {alpha * acc.x, alpha * acc.y, alpha * acc.z, alpha * acc.w};
-      if (beta != 0.f)
+      if (beta != 0.f) {
+#pragma unroll
         for (int j = 0; j < 4; ++j) v[j] += beta * E::to_f32(c[j]);
+      }
       if ((reinterpret_cast<uintptr_t>(c) & 7u) == 0) {
         uint2 w;
         w.x = E::pack(v[0], v[1]);
         w.y = E::pack(v[2], v[3]);
         *reinterpret_cast<uint2*>(c) = w;
       } else {
+#pragma unroll
         for (int j = 0; j < 4; ++j) c[j] = E::from_f32(v[j]);
       }
     } else {
-      const float acc = sum_slots(part + off, plane, S);  // in split order
       float v = alpha * acc;
       if (beta != 0.f) v += beta * E::to_f32(*c);
       *c = E::from_f32(v);
@@ -122,21 +158,27 @@ cudaError_t launch_reduce(const float* part, int S, const GemmParams& p, cudaStr
   const gpu::Target* d = gpu::this_device();
   const int sms = d ? d->sms : 148;
   const bool vec = p.N % 4 == 0;
-  const long long total = (long long)p.batch * p.M * (vec ? p.N / 4 : p.N);
-  const int blocks = int(std::max<long long>(1, std::min<long long>((total + 255) / 256, (long long)sms * 8)));
+  const long long plane = (long long)p.batch * p.M * p.N;
+  if ((long long)S * plane >= (1ll << 31)) return cudaErrorInvalidValue;  // beyond the workspace cap
+  const int G = reduce_groups(S);
+  int lg = 0;
+  while ((1 << lg) < G) ++lg;
+  const int U = kReduceThreads >> lg;
+  const long long total = vec ? plane / 4 : plane;
+  const int blocks = int(std::max<long long>(1, std::min<long long>((total + U - 1) / U, (long long)sms * 8)));
   T* C = static_cast<T*>(p.C);
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(unsigned(blocks));
-  cfg.blockDim = dim3(256);
+  cfg.blockDim = dim3(kReduceThreads);
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return vec ? cudaLaunchKernelEx(&cfg, &splitk_reduce_kernel<T, true>, part, S, p.batch, p.M, p.N, C, p.ldc,
+  return vec ? cudaLaunchKernelEx(&cfg, &splitk_reduce_kernel<T, true>, part, S, lg, p.batch, p.M, p.N, C, p.ldc,
                                   p.stride_c, p.alpha, p.beta)
-             : cudaLaunchKernelEx(&cfg, &splitk_reduce_kernel<T, false>, part, S, p.batch, p.M, p.N, C, p.ldc,
+             : cudaLaunchKernelEx(&cfg, &splitk_reduce_kernel<T, false>, part, S, lg, p.batch, p.M, p.N, C, p.ldc,
                                   p.stride_c, p.alpha, p.beta);
 }
 
@@ -249,6 +291,12 @@ Plan make_plan(int cfg, const GemmParams& p) {
     const double reduce_ns = out_elems * 8.0 / 5.0e3;
     const long long cap = std::max<long long>(1, gemm::kSplitKMaxWorkspace / (long long)std::max(1.0, out_elems * 4));
     S = splitk_choose(pl.tiles, pl.kb_total, sms, 4, t_block_ns, reduce_ns, cap);
+    // AEGIS_UMMA_SPLITS overrides the model for tuning sweeps (read on every
+    // plan; clamped to [1, k-blocks / 4] and the workspace cap).
+    if (const char* env = std::getenv("AEGIS_UMMA_SPLITS")) {
+      const long long v = std::atoll(env);
+      if (v >= 1) S = int(std::max<long long>(1, std::min<long long>({v, pl.kb_total / 4, cap})));
+    }
   }
   pl.slots = sms;
   pl.kb_per_split = ceil_div(pl.kb_total, S);

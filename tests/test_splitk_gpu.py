@@ -75,6 +75,34 @@ def test_split_shapes_layouts(cuda, shape, impl):
     check(d, A, B, C0, outs[0], op.gemm_ref(d, A, B, C0 if beta != 0 else None), f"{impl} {shape}")
 
 
+@pytest.mark.parametrize("shape", [(256, 256, 20480, 0.0), (200, 262, 20480, 0.5)])
+@pytest.mark.parametrize("impl", ["umma_128x128x64_s6_ksm", "umma_256x256x64_s7_c2_ksm"])
+def test_forced_split_counts(cuda, monkeypatch, shape, impl):
+    """Every slot-group count of the reduce (1, 2, 4, 8 groups; the last group
+    short; more than 8 slots per group past S = 64), float4 and scalar columns
+    (N % 4 == 0 and N = 262), with beta: bitwise repeatable and within the
+    oracle's tolerance. AEGIS_UMMA_SPLITS sets the split count."""
+    torch = cuda
+    M, N, K, beta = shape
+    d = op.make_desc(M, N, K, 0, 0, K, N, N, 1.0, beta, 1, 0, 0, 0, "bf16")
+    g = ac.Generator(M + N + K)
+    A, B, C0 = g.uniform(M * K, "bf16"), g.uniform(K * N, "bf16"), g.uniform(M * N, "bf16")
+    ctx = context(torch)
+    dA, dB = dev(torch, A), dev(torch, B)
+    ref = op.gemm_ref(d, A, B, C0 if beta != 0 else None)
+    # 320 k-blocks: each count is ceil(320 / ceil(320 / S)), so the plan keeps it.
+    for S in [2, 7, 9, 16, 17, 40, 64, 80]:
+        monkeypatch.setenv("AEGIS_UMMA_SPLITS", str(S))
+        assert ctx.plan(M, N, K, impl, ac.DTYPE_BF16)["splits"] == S
+        outs = []
+        for _ in range(2):
+            dC = dev(torch, C0)
+            run(torch, ctx, d, dA, dB, dC, impl)
+            outs.append(host(dC))
+        assert np.array_equal(outs[0], outs[1]), (impl, S)
+        check(d, A, B, C0, outs[0], ref, f"{impl} S={S} {shape}")
+
+
 def test_odd_split_counts_occur(cuda):
     ctx = context(cuda)
     counts = {ctx.plan(m, n, k, impl)["splits"] for impl in SPLIT_IMPLS
