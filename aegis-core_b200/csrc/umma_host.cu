@@ -406,8 +406,10 @@ cudaError_t umma_attrs(int cfg, cudaFuncAttributes* attrs) {
 size_t umma_smem_bytes(int cfg) {
   const gemm::UmmaConfig& c = gemm::UMMA_CONFIGS[cfg];
   if (c.CTAS == 2) return size_t(umma::LayoutPair<256, gemm::kUmmaPairStages>::ALLOC);
-  if (c.BN == 64) return size_t(umma::Layout<64, 8>::ALLOC);
-  return c.BN == 256 ? size_t(umma::Layout<256, 4>::ALLOC) : size_t(umma::Layout<128, 6>::ALLOC);
+  // Split-K configs also launch the partial-store epilogue, with its staging.
+  const int epi = c.SPLITK ? umma::kEpiPartial : umma::kEpiStore;
+  if (c.BN == 64) return size_t(umma::Layout<64, 8>::alloc_for(epi));
+  return c.BN == 256 ? size_t(umma::Layout<256, 4>::alloc_for(epi)) : size_t(umma::Layout<128, 6>::alloc_for(epi));
 }
 
 cudaError_t umma_nsharded(const GemmParams& local, void* const* c_ranks, int nranks, int col_offset,

@@ -95,6 +95,13 @@ struct Layout {
   static constexpr int SCHED_OFF = (MISC_OFF + 16 + 15) / 16 * 16;  // tile schedule (tile_sched.cuh)
   static constexpr int BYTES = SCHED_OFF + SchedSmem::BYTES;
   static constexpr int ALLOC = BYTES + 1024;  // dynamic smem requested (1024-byte alignment slack)
+  // Split-K partial store staging (kEpiPartial launches only): 4 KB per
+  // epilogue warp (32 rows x 128 bytes) after the schedule state. The other
+  // epilogues do not request it: the spare shared memory stays L1.
+  static constexpr int EPI_WARP_BYTES = 4096;
+  static constexpr int EPI_OFF = (BYTES + 127) / 128 * 128;
+  static constexpr int ALLOC_STAGED = EPI_OFF + 4 * EPI_WARP_BYTES + 1024;
+  static constexpr int alloc_for(int epi) { return epi == kEpiPartial ? ALLOC_STAGED : ALLOC; }
   static constexpr int TMEM_COLS = 2 * BN;
   static_assert(A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "tiles must stay 1024-byte aligned");
   static_assert(TMEM_COLS >= 32 && TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0,
@@ -310,27 +317,73 @@ __device__ __forceinline__ void push_warp_rows(const Args& a, const Unit& u, int
   }
 }
 
+// Warp-wide split-K partial store of one 32-column FP32 chunk through a 4 KB
+// shared-memory buffer at `stage`: each lane holds one row (row_first + lane)
+// in the TMEM layout; the chunk is written to shared memory row by row and
+// stored back with the lanes across the columns, so each 16-byte store of the
+// warp lands in whole 128-byte row segments (4 rows per instruction: 8x fewer
+// store requests than 16-byte pieces of 32 rows). The 16-byte slots of a row
+// are XOR-swizzled by the row, so both shared-memory passes take the minimum
+// four wavefronts. Measured on a B200 (graph windows, cold L2, bitwise equal
+// outputs): 256^2 x 65536 split-K 21.2 -> 20.6 us, 512^2 x 65536 43.0 -> 40.9
+// us. 16-bit C stores stay per row: staged they were 3-6% slower on 512^3 to
+// 2048^3 (the extra shared-memory round trip sits on the critical path of a
+// one-tile CTA), and so were warps with fewer than 32 rows inside M. The
+// caller takes this path only for full warps of full chunks (warp-uniform).
+template <class T>
+__device__ __forceinline__ void partial_chunk_staged(const Args& a, const Unit& u, int row_first, int lane, int col,
+                                                     const uint32_t (&r)[32], uint32_t stage) {
+  float* plane = a.partials + ((long long)u.split * a.batch + u.b) * a.M * (long long)a.N;
+#pragma unroll
+  for (int q = 0; q < 8; ++q)
+    ptx::st_shared_v4(stage + uint32_t(lane * 128 + 16 * (q ^ (lane & 7))), r[4 * q], r[4 * q + 1], r[4 * q + 2],
+                      r[4 * q + 3]);
+  __syncwarp();
+  const int q = lane & 7;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int rl = 4 * j + (lane >> 3);
+    const uint4 v = ptx::ld_shared_v4(stage + uint32_t(rl * 128 + 16 * (q ^ (rl & 7))));
+    *reinterpret_cast<uint4*>(plane + (long long)(row_first + rl) * a.N + col + 4 * q) = v;
+  }
+  __syncwarp();  // the buffer is rewritten by the next chunk
+}
+
 // Reads this warp's 32 rows of a BN-column accumulator from TMEM and hands
 // each 32-column chunk to the epilogue. Two register buffers: the next
 // chunk's TMEM load is in flight while the current one is converted and
 // stored, so a tile costs about one load latency instead of BN/32 of them
 // (tcgen05.wait::ld waits for every load this thread has issued, and only
 // one is outstanding at each wait). ld and wait run on the whole warp.
+// `stage`: this warp's 4 KB staging buffer for split-K partials
+// (partial_chunk_staged), or 0 to store each row from its own lane.
 template <class T, int EPI, int BN>
-__device__ __forceinline__ void drain_rows(const Args& a, const Unit& u, int row, uint32_t t_row) {
+__device__ __forceinline__ void drain_rows(const Args& a, const Unit& u, int row, uint32_t t_row,
+                                           uint32_t stage = 0) {
   static_assert(BN % 64 == 0, "chunks are taken in pairs");
   uint32_t r0[32], r1[32];
+  const int lane = int(threadIdx.x & 31);
+  const int row_first = row - lane;
+  // Staged partial stores: the whole warp's 32 rows inside M, rows 16-byte
+  // aligned (N % 4 == 0; the scratch base is 256-byte aligned). Warp-uniform.
+  const bool staged = EPI == kEpiPartial && stage != 0 && row_first + 32 <= a.M && (a.N & 3) == 0;
   ptx::tmem_ld_32x32b_x32(t_row, r0);
 #pragma unroll 1
   for (int c = 0; c < BN / 32; c += 2) {
     ptx::tmem_ld_wait(r0);
     ptx::tmem_ld_32x32b_x32(t_row + uint32_t((c + 1) * 32), r1);
     const int col0 = u.n0 + c * 32;
-    if (row < a.M && col0 < a.N) epilogue_chunk<T, EPI>(a, u, row, col0, r0);
+    if (staged && col0 + 32 <= a.N)
+      partial_chunk_staged<T>(a, u, row_first, lane, col0, r0, stage);
+    else if (row < a.M && col0 < a.N)
+      epilogue_chunk<T, EPI>(a, u, row, col0, r0);
     ptx::tmem_ld_wait(r1);
     if (c + 2 < BN / 32) ptx::tmem_ld_32x32b_x32(t_row + uint32_t((c + 2) * 32), r0);
     const int col1 = col0 + 32;
-    if (row < a.M && col1 < a.N) epilogue_chunk<T, EPI>(a, u, row, col1, r1);
+    if (staged && col1 + 32 <= a.N)
+      partial_chunk_staged<T>(a, u, row_first, lane, col1, r1, stage);
+    else if (row < a.M && col1 < a.N)
+      epilogue_chunk<T, EPI>(a, u, row, col1, r1);
   }
 }
 
@@ -521,7 +574,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::tc_fence_after();
       const int row = u.m0 + row_in_tile;
       const uint32_t t_row = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN);
-      drain_rows<T, EPI, BN>(a, u, row, t_row);
+      drain_rows<T, EPI, BN>(a, u, row, t_row,
+                             EPI == kEpiPartial ? sbase + uint32_t(L::EPI_OFF + quarter * L::EPI_WARP_BYTES) : 0u);
       ptx::tc_fence_before();
       ptx::mbar_arrive(tempty_bar(acc));
       acc ^= 1;

@@ -22,7 +22,7 @@ cudaError_t launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const Args&
                        cudaStream_t stream) {
   auto* kern = &umma_gemm_kernel<T, BN, STAGES, A_MN, B_MN, EPI>;
   static gpu::SmemOptIn optin;
-  constexpr size_t smem = size_t(Layout<BN, STAGES>::ALLOC);
+  constexpr size_t smem = size_t(Layout<BN, STAGES>::alloc_for(EPI));
   if (const cudaError_t e = optin.ensure(reinterpret_cast<const void*>(kern), smem); e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(unsigned(grid));
@@ -64,7 +64,7 @@ cudaError_t launch_one_pair(const CUtensorMap& ta, const CUtensorMap& tb, const 
 template <class T, int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
 cudaError_t attrs_one(cudaFuncAttributes* attrs) {
   const cudaError_t e = cudaFuncGetAttributes(attrs, &umma_gemm_kernel<T, BN, STAGES, A_MN, B_MN, EPI>);
-  if (e == cudaSuccess) attrs->sharedSizeBytes += Layout<BN, STAGES>::ALLOC;
+  if (e == cudaSuccess) attrs->sharedSizeBytes += Layout<BN, STAGES>::alloc_for(EPI);
   return e;
 }
 
