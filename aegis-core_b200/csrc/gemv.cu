@@ -16,14 +16,22 @@
 //   - FP32 FMA into MT x 8 accumulators per thread, k ascending.
 //   - Reduction: row groups inside a warp by a fixed shuffle-xor tree, then
 //     the 8 warps through shared memory in warp order 0..7.
-//   - Split-K, deterministic (reference src/gemm/splitk.cuh:155-222): every
-//     CTA of a tile writes its FP32 partial slot, fences, takes a ticket on
-//     the tile's counter; the CTA that draws the last ticket sums slots
-//     0..S-1 in order, applies alpha/beta, and resets the counter to 0.
-//     Nothing waits on another CTA.
+//   - Split-K, deterministic. With S = 2, 4 or 8 splits the tile's S CTAs form one
+//     thread-block cluster (split = cluster rank): each leaves its FP32
+//     partial in its own shared memory, and after a cluster barrier rank 0
+//     sums ranks 0..S-1 in order over distributed shared memory and applies
+//     alpha/beta. With more splits (reference src/gemm/splitk.cuh:155-222):
+//     every CTA of a tile writes its FP32 partial slot, fences, takes a
+//     ticket on the tile's counter; the CTA that draws the last ticket sums
+//     slots 0..S-1 in order, applies alpha/beta, and resets the counter to 0.
+//     Either way the order is fixed and nothing spins on another CTA.
 // No tensor cores: the shape is memory-bound.
 #include <algorithm>
+#include <cstdlib>
+#include <map>
 #include <mutex>
+#include <tuple>
+#include <type_traits>
 
 #include "common.cuh"
 #include "gpu_target.h"
@@ -61,9 +69,10 @@ struct GemvArgs {
   float alpha, beta;
   int tiles_n, tiles_m;
   int S, kc;                 // splits, rows per split
-  unsigned* counters;        // per tile (S > 1)
-  float* partials;           // tiles x S x MT x BN (S > 1)
+  unsigned* counters;        // per tile (S > 1, ticket fix-up)
+  float* partials;           // tiles x S x MT x BN (S > 1, ticket fix-up)
   int batch0;
+  int cluster;               // 1: launched in clusters of S CTAs (S = 2, 4, 8), fix-up in shared memory
 };
 
 template <int MT>
@@ -258,6 +267,39 @@ __global__ void __launch_bounds__(GThreads, gemv_ctas_per_sm(MT)) gemv_kernel(Ge
     }
     return;
   }
+  if (a.cluster) {
+    // The tile's S CTAs are one cluster, rank = split (grid x = tiles_n * S,
+    // cluster dims (S, 1, 1)). Every thread of every CTA passes both
+    // barriers: the first publishes each CTA's partial (release/acquire at
+    // cluster scope), the second keeps every CTA resident until rank 0 has
+    // read its shared memory.
+    __syncthreads();  // every warp is done reading the cross-warp sums
+#pragma unroll
+    for (int r = 0; r < ceil_div(ELEMS, GThreads); ++r) {
+      const int e = tid + r * GThreads;
+      if (e < ELEMS) sm[e] = tilev[r];
+    }
+    ptx::cluster_sync();
+    if (ptx::cluster_ctarank() == 0) {
+#pragma unroll
+      for (int r = 0; r < ceil_div(ELEMS, GThreads); ++r) {
+        const int e = tid + r * GThreads;
+        if (e >= ELEMS) continue;
+        const uint32_t local = ptx::smem_addr(&sm[e]);
+        float v[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          if (q < a.S) v[q] = ptx::ld_shared_cluster_f32(ptx::map_to_rank(local, uint32_t(q)));
+        float sum = v[0];
+#pragma unroll
+        for (int q = 1; q < 8; ++q)
+          if (q < a.S) sum += v[q];
+        store(e, sum);
+      }
+    }
+    ptx::cluster_sync();
+    return;
+  }
   const long long tile = ((long long)blockIdx.z * a.tiles_m + mt) * a.tiles_n + nt;
   float* slot0 = a.partials + tile * a.S * ELEMS;
 #pragma unroll
@@ -304,6 +346,54 @@ struct GPlan {
   long long tiles;
 };
 
+// Cluster split-K fix-up (the kernel's a.cluster path) for S = 2, 4 or 8.
+// Against the global-ticket fix-up on a B200 (graph windows, three
+// alternating runs): clusters of 2, 4 and 8 were 1-4.5% faster or level;
+// 112 clusters of 5 (M = 1, N x K = 14336 x 4096, BN = 128) were 11% slower,
+// so other split counts keep the ticket fix-up. AEGIS_GEMV_CLUSTER=0 turns
+// it off (global-ticket fix-up for every S, no split trimming), read once,
+// for A/B measurement.
+bool gemv_clusters_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("AEGIS_GEMV_CLUSTER");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+constexpr int kMaxClusterSplits = 8;
+
+// The clusters of S CTAs the device can hold at once for `kernel`
+// (cudaOccupancyMaxActiveClusters), cached per (device, kernel, S); 0 when
+// the query fails. A cluster must fit one GPC, so clusters of S CTAs can hold
+// fewer CTAs than the per-SM limit suggests: a launch uses the cluster fix-up
+// only when all its clusters fit at once.
+int max_active_clusters(const void* kernel, int S) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, const void*, int>, int> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  const auto key = std::make_tuple(dev, kernel, S);
+  std::lock_guard<std::mutex> lock(mu);
+  if (const auto it = cache.find(key); it != cache.end()) return it->second;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(unsigned(S));
+  cfg.blockDim = dim3(GThreads);
+  cfg.dynamicSmemBytes = 0;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = unsigned(S);
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess) {
+    (void)cudaGetLastError();  // the query failed: no cluster fix-up, nothing left pending
+    n = 0;
+  }
+  return cache[key] = n;
+}
+
 GPlan plan_for(int cfg, const GemmParams& p) {
   const gemm::GemvConfig& c = gemm::GEMV_CONFIGS[cfg];
   GPlan pl{};
@@ -322,6 +412,14 @@ GPlan plan_for(int cfg, const GemmParams& p) {
   // M = 16, K x N = 4096 x 14336 on 74 SMs).
   const long long target = (long long)sms * gemv_ctas_per_sm(pl.MT);
   long long S = std::max<long long>(1, target / pl.tiles);  // rounded down: never a second wave
+  // Nine splits become eight, the largest cluster fix-up (portable cluster
+  // size), at MT <= 2: a ninth of the CTAs for a tail without the global
+  // ticket round trips. Measured on a B200 (graph windows): M = 1, K x N =
+  // 4096 x 4096, BN = 64: 10.09 -> 9.31 us; M = 2: 12.24 -> 12.02 us. Not
+  // kept: ten splits to eight (BN = 256, N = 14336: 0.7% slower) and nine to
+  // eight at M = 4 (15.87 -> 16.34 us: the longer slices cost more than the
+  // tail saves).
+  if (gemv_clusters_enabled() && pl.MT <= 2 && S == 9) S = 8;
   S = std::min<long long>(S, std::max(1, ceil_div(p.K, 64)));
   // Rows per split: ceil(K / S) rounded up to 16, in 64-bit (K may be near
   // 2^31); a split of all of K when rounding would pass K.
@@ -354,11 +452,18 @@ cudaError_t launch_t(const GemvArgs& a, dim3 grid, cudaStream_t s) {
   cfg.blockDim = dim3(GThreads);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (a.cluster) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = unsigned(a.S);
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
+  }
   return cudaLaunchKernelEx(&cfg, &gemv_kernel<T, LPR, MT, VECB>, a);
 }
 
@@ -392,6 +497,38 @@ cudaError_t launch_lpr(int LPR, int MT, const GemvArgs& a, dim3 grid, cudaStream
 template <class T>
 cudaError_t launch_all(bool vec, int LPR, int MT, const GemvArgs& a, dim3 grid, cudaStream_t s) {
   return vec ? launch_lpr<T, true>(LPR, MT, a, grid, s) : launch_lpr<T, false>(LPR, MT, a, grid, s);
+}
+
+template <class T, int LPR, bool VECB>
+const void* kernel_mt(int MT) {
+  switch (MT) {
+    case 1: return reinterpret_cast<const void*>(&gemv_kernel<T, LPR, 1, VECB>);
+    case 2: return reinterpret_cast<const void*>(&gemv_kernel<T, LPR, 2, VECB>);
+    case 4: return reinterpret_cast<const void*>(&gemv_kernel<T, LPR, 4, VECB>);
+    case 8:
+      if constexpr (LPR <= 16) return reinterpret_cast<const void*>(&gemv_kernel<T, LPR, 8, VECB>);
+      break;
+    case 16:
+      if constexpr (LPR <= 8) return reinterpret_cast<const void*>(&gemv_kernel<T, LPR, 16, VECB>);
+      break;
+  }
+  return nullptr;
+}
+
+// The kernel instantiation launch_all runs for these parameters.
+template <class T>
+const void* kernel_for(bool vec, int LPR, int MT) {
+  auto by_lpr = [&](auto vecb) -> const void* {
+    constexpr bool V = decltype(vecb)::value;
+    switch (LPR) {
+      case 32: return kernel_mt<T, 32, V>(MT);
+      case 16: return kernel_mt<T, 16, V>(MT);
+      case 8: return kernel_mt<T, 8, V>(MT);
+      case 4: return kernel_mt<T, 4, V>(MT);
+    }
+    return nullptr;
+  };
+  return vec ? by_lpr(std::true_type{}) : by_lpr(std::false_type{});
 }
 
 constexpr int kMaxGridZ = 65535;
@@ -428,10 +565,18 @@ cudaError_t gemv_run(int cfg, const GemmParams& p, cudaStream_t stream) {
   const long long grid_x = (long long)pl.tiles_n * pl.S;
   if (grid_x > 0x7fffffffll) return cudaErrorInvalidConfiguration;
   const bool vec = vec_b_ok(p);
+  const bool cluster_ok =
+      gemv_clusters_enabled() && (pl.S == 2 || pl.S == 4 || pl.S == kMaxClusterSplits);
+  const int cluster_cap =
+      cluster_ok ? max_active_clusters(p.dtype == DType::BF16 ? kernel_for<__nv_bfloat16>(vec, pl.LPR, pl.MT)
+                                                               : kernel_for<__half>(vec, pl.LPR, pl.MT),
+                                       pl.S)
+                 : 0;
   for (int b0 = 0; b0 < p.batch; b0 += kMaxGridZ) {
     const int nb = std::min(kMaxGridZ, p.batch - b0);
     a.batch0 = b0;
-    if (pl.S > 1) {
+    a.cluster = cluster_ok && (long long)pl.tiles_n * pl.tiles_m * nb <= cluster_cap;
+    if (pl.S > 1 && !a.cluster) {
       // Tile indices restart per launch (blockIdx.z), so each launch of a
       // batch chunk reuses the same counter/partial slots, in stream order.
       const long long tiles = (long long)pl.tiles_n * pl.tiles_m * nb;
