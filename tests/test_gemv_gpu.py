@@ -80,3 +80,44 @@ def test_gemv_bf16(cuda):
         dA, dB, dC = dev(torch, A), dev(torch, B), dev(torch, np.zeros(M * N, np.uint16))
         run(torch, ctx, d, dA, dB, dC, impl)
         check(d, A, B, None, host(dC), op.gemm_ref(d, A, B), str(impl))
+
+
+# (impl, M, N, K, splits per tile): gemv plans of 2, 4 and 8 splits (the
+# cluster split-K fix-up, every cluster size) and tile-aligned ummav grids of
+# 2, 4 and 8 segments per tile (ordered tickets), with beta on half of them.
+CLUSTER_CASES = [
+    ("ummav_128x16x64_s6x2", 1, 14336, 4096, 2),
+    ("ummav_128x16x64_s6x2", 3, 9472, 2048, 4),
+    ("ummav_128x16x64_s6x2", 16, 4736, 4096, 8),
+    ("ummav_128x16x64_s11", 5, 4736, 2048, 4),
+    ("ummav_128x16x64_s11", 1, 2304, 8192, 8),
+    ("gemv_64x256_ksm", 1, 4096, 4096, 8),
+    ("gemv_64x256_ksm", 2, 9472, 2048, 4),
+    ("gemv_128x256_ksm", 1, 37888, 1024, 2),
+]
+
+
+@pytest.mark.parametrize("impl,M,N,K,s", CLUSTER_CASES)
+def test_cluster_fixup(cuda, impl, M, N, K, s):
+    """Split fix-ups at s = 2, 4, 8 splits per tile (gemv: inside a
+    thread-block cluster; ummav: grid = tiles x s, ordered tickets): results
+    bitwise repeatable and within the oracle's bounds, with and without beta."""
+    torch = cuda
+    ctx = context(torch)
+    p = ctx.plan(M, N, K, impl, ac.DTYPE_F16)
+    if impl.startswith("ummav"):  # its plan reports a bound on segments per tile; the grid shows s
+        assert p["grid"] == p["tiles"] * s, p
+    else:
+        assert p["splits"] == s, p
+    beta = 0.5 if (M + s) % 2 else 0.0
+    d = op.make_desc(M, N, K, 0, 0, K, N, N, 1.5, beta, 1, 0, 0, 0, "f16")
+    g = ac.Generator(M * 7 + s)
+    A, B, C0 = g.uniform(M * K), g.uniform(K * N), g.uniform(M * N)
+    dA, dB = dev(torch, A), dev(torch, B)
+    outs = []
+    for _ in range(2):
+        dC = dev(torch, C0)
+        run(torch, ctx, d, dA, dB, dC, impl)
+        outs.append(host(dC))
+    assert np.array_equal(outs[0], outs[1]), impl
+    check(d, A, B, C0, outs[0], op.gemm_ref(d, A, B, C0 if beta != 0 else None), f"{impl} {M}x{N}x{K} s={s}")
