@@ -148,9 +148,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     s.nkb = int(min(unsigned(a.kb - s.kb0), r1 - pos));
     return s;
   };
-  if (warp == 0 && lane == 0) {
+  if (STAGES < 8 && warp == 0 && lane == 0) {
     // The weights of this CTA's first STAGES k-blocks into L2 while the
     // previous grid ends (ptx::tma_prefetch_3d: a hint, safe before the wait).
+    // Shallow rings only. A/B on a B200 (graph windows, eight decode shapes):
+    // with it the 6-stage config (two CTAs per SM) ran 4-8% faster, the
+    // 11-stage one (one CTA per SM) ~2% slower on six of eight: its own ring
+    // already covers the start, and the prefetches add L2 requests.
     int n = 0;
     for (unsigned pos = r0; pos < r1 && n < STAGES;) {
       const Seg sg = next_seg(pos);
