@@ -308,3 +308,18 @@ def test_k_walk_by_wave_only_on_unsplit_multi_wave_launches(shape):
     assert kw["kdir_wave"] == (74 if kw["splits"] == 1 and kw["tiles"] > 74 else 0), kw
     for impl in ["umma_128x256x64_s4", "umma_128x128x64_s6_ksm", "umma_256x256x64_s7_c2_ksm", "umma_128x64x64_s8"]:
         assert plan(*shape, impl=impl)["kdir_wave"] == 0
+
+
+def test_gemv_nine_splits_become_eight_at_small_m():
+    """The cluster split-K fix-up takes at most 8 splits (portable cluster
+    size): at MT <= 2 a plan of nine splits is trimmed to eight; at M = 4 the
+    split count stays (measured slower trimmed). 4096 x 4096 with 64-column
+    tiles: 64 tiles x 9 = 576 CTAs would fill 592 slots."""
+    for M in (1, 2):
+        p = plan(M, 4096, 4096, "gemv_64x256_ksm")
+        assert p["splits"] == 8 and p["grid"] == 64 * 8, p
+    p = plan(4, 4096, 4096, "gemv_64x256_ksm")
+    assert p["splits"] == 9 and p["grid"] == 64 * 9, p
+    # Ten splits are not trimmed (64 x 10 <= 148 x 4 needs N = 3648: 57 tiles -> 10 splits).
+    p = plan(1, 3648, 4096, "gemv_64x256_ksm")
+    assert p["splits"] == 10, p
