@@ -441,12 +441,48 @@ bool vec_b_ok(const GemmParams& p) {
          (p.batch <= 1 || p.stride_b % 8 == 0);
 }
 
+template <class T, int LPR, bool VECB>
+const void* kernel_mt(int MT) {
+  switch (MT) {
+    case 1: return reinterpret_cast<const void*>(&gemv_kernel<T, LPR, 1, VECB>);
+    case 2: return reinterpret_cast<const void*>(&gemv_kernel<T, LPR, 2, VECB>);
+    case 4: return reinterpret_cast<const void*>(&gemv_kernel<T, LPR, 4, VECB>);
+    case 8:
+      if constexpr (LPR <= 16) return reinterpret_cast<const void*>(&gemv_kernel<T, LPR, 8, VECB>);
+      break;
+    case 16:
+      if constexpr (LPR <= 8) return reinterpret_cast<const void*>(&gemv_kernel<T, LPR, 16, VECB>);
+      break;
+  }
+  return nullptr;
+}
+
+// The gemv_kernel instantiation for these parameters (nullptr: none).
+template <class T>
+const void* kernel_for(bool vec, int LPR, int MT) {
+  auto by_lpr = [&](auto vecb) -> const void* {
+    constexpr bool V = decltype(vecb)::value;
+    switch (LPR) {
+      case 32: return kernel_mt<T, 32, V>(MT);
+      case 16: return kernel_mt<T, 16, V>(MT);
+      case 8: return kernel_mt<T, 8, V>(MT);
+      case 4: return kernel_mt<T, 4, V>(MT);
+    }
+    return nullptr;
+  };
+  return vec ? by_lpr(std::true_type{}) : by_lpr(std::false_type{});
+}
+
+const void* kernel_for(DType dt, bool vec, int LPR, int MT) {
+  return dt == DType::BF16 ? kernel_for<__nv_bfloat16>(vec, LPR, MT) : kernel_for<__half>(vec, LPR, MT);
+}
+
 // Launched with programmatic stream serialization: the grid may start while
 // the previous grid on the stream drains; it waits (griddepcontrol.wait)
 // before its first global read and lets its own dependents launch once its
-// weight loads are in flight.
-template <class T, int LPR, int MT, bool VECB>
-cudaError_t launch_t(const GemvArgs& a, dim3 grid, cudaStream_t s) {
+// weight loads are in flight. a.cluster: clusters of a.S CTAs along x.
+cudaError_t launch(const void* kernel, const GemvArgs& a, dim3 grid, cudaStream_t s) {
+  if (!kernel) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(GThreads);
@@ -464,71 +500,9 @@ cudaError_t launch_t(const GemvArgs& a, dim3 grid, cudaStream_t s) {
     attr[1].val.clusterDim.z = 1;
     cfg.numAttrs = 2;
   }
-  return cudaLaunchKernelEx(&cfg, &gemv_kernel<T, LPR, MT, VECB>, a);
-}
-
-template <class T, int LPR, bool VECB>
-cudaError_t launch_mt(int MT, const GemvArgs& a, dim3 grid, cudaStream_t s) {
-  switch (MT) {
-    case 1: return launch_t<T, LPR, 1, VECB>(a, grid, s);
-    case 2: return launch_t<T, LPR, 2, VECB>(a, grid, s);
-    case 4: return launch_t<T, LPR, 4, VECB>(a, grid, s);
-    case 8:
-      if constexpr (LPR <= 16) return launch_t<T, LPR, 8, VECB>(a, grid, s);
-      break;
-    case 16:
-      if constexpr (LPR <= 8) return launch_t<T, LPR, 16, VECB>(a, grid, s);
-      break;
-  }
-  return cudaErrorInvalidValue;
-}
-
-template <class T, bool VECB>
-cudaError_t launch_lpr(int LPR, int MT, const GemvArgs& a, dim3 grid, cudaStream_t s) {
-  switch (LPR) {
-    case 32: return launch_mt<T, 32, VECB>(MT, a, grid, s);
-    case 16: return launch_mt<T, 16, VECB>(MT, a, grid, s);
-    case 8: return launch_mt<T, 8, VECB>(MT, a, grid, s);
-    case 4: return launch_mt<T, 4, VECB>(MT, a, grid, s);
-  }
-  return cudaErrorInvalidValue;
-}
-
-template <class T>
-cudaError_t launch_all(bool vec, int LPR, int MT, const GemvArgs& a, dim3 grid, cudaStream_t s) {
-  return vec ? launch_lpr<T, true>(LPR, MT, a, grid, s) : launch_lpr<T, false>(LPR, MT, a, grid, s);
-}
-
-template <class T, int LPR, bool VECB>
-const void* kernel_mt(int MT) {
-  switch (MT) {
-    case 1: return reinterpret_cast<const void*>(&gemv_kernel<T, LPR, 1, VECB>);
-    case 2: return reinterpret_cast<const void*>(&gemv_kernel<T, LPR, 2, VECB>);
-    case 4: return reinterpret_cast<const void*>(&gemv_kernel<T, LPR, 4, VECB>);
-    case 8:
-      if constexpr (LPR <= 16) return reinterpret_cast<const void*>(&gemv_kernel<T, LPR, 8, VECB>);
-      break;
-    case 16:
-      if constexpr (LPR <= 8) return reinterpret_cast<const void*>(&gemv_kernel<T, LPR, 16, VECB>);
-      break;
-  }
-  return nullptr;
-}
-
-// The kernel instantiation launch_all runs for these parameters.
-template <class T>
-const void* kernel_for(bool vec, int LPR, int MT) {
-  auto by_lpr = [&](auto vecb) -> const void* {
-    constexpr bool V = decltype(vecb)::value;
-    switch (LPR) {
-      case 32: return kernel_mt<T, 32, V>(MT);
-      case 16: return kernel_mt<T, 16, V>(MT);
-      case 8: return kernel_mt<T, 8, V>(MT);
-      case 4: return kernel_mt<T, 4, V>(MT);
-    }
-    return nullptr;
-  };
-  return vec ? by_lpr(std::true_type{}) : by_lpr(std::false_type{});
+  GemvArgs args = a;
+  void* params[] = {&args};
+  return cudaLaunchKernelExC(&cfg, kernel, params);
 }
 
 constexpr int kMaxGridZ = 65535;
@@ -565,13 +539,10 @@ cudaError_t gemv_run(int cfg, const GemmParams& p, cudaStream_t stream) {
   const long long grid_x = (long long)pl.tiles_n * pl.S;
   if (grid_x > 0x7fffffffll) return cudaErrorInvalidConfiguration;
   const bool vec = vec_b_ok(p);
+  const void* kernel = kernel_for(p.dtype, vec, pl.LPR, pl.MT);
   const bool cluster_ok =
       gemv_clusters_enabled() && (pl.S == 2 || pl.S == 4 || pl.S == kMaxClusterSplits);
-  const int cluster_cap =
-      cluster_ok ? max_active_clusters(p.dtype == DType::BF16 ? kernel_for<__nv_bfloat16>(vec, pl.LPR, pl.MT)
-                                                               : kernel_for<__half>(vec, pl.LPR, pl.MT),
-                                       pl.S)
-                 : 0;
+  const int cluster_cap = cluster_ok && kernel ? max_active_clusters(kernel, pl.S) : 0;
   for (int b0 = 0; b0 < p.batch; b0 += kMaxGridZ) {
     const int nb = std::min(kMaxGridZ, p.batch - b0);
     a.batch0 = b0;
@@ -591,8 +562,7 @@ cudaError_t gemv_run(int cfg, const GemmParams& p, cudaStream_t stream) {
       a.partials = static_cast<float*>(part);
     }
     const dim3 grid(unsigned(grid_x), unsigned(pl.tiles_m), unsigned(nb));
-    const cudaError_t e = p.dtype == DType::BF16 ? launch_all<__nv_bfloat16>(vec, pl.LPR, pl.MT, a, grid, stream)
-                                                 : launch_all<__half>(vec, pl.LPR, pl.MT, a, grid, stream);
+    const cudaError_t e = launch(kernel, a, grid, stream);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
@@ -743,8 +713,7 @@ cudaError_t gemv_run_noalloc(const GemmParams& p, cudaStream_t stream, const cha
       return e;
   }
   const dim3 grid(unsigned((long long)pl.tiles_n * pl.S), unsigned(pl.tiles_m), 1u);
-  return p.dtype == DType::BF16 ? launch_all<__nv_bfloat16>(vec_b_ok(p), pl.LPR, pl.MT, a, grid, stream)
-                                : launch_all<__half>(vec_b_ok(p), pl.LPR, pl.MT, a, grid, stream);
+  return launch(kernel_for(p.dtype, vec_b_ok(p), pl.LPR, pl.MT), a, grid, stream);
 }
 
 }  // namespace aegis
